@@ -1,0 +1,100 @@
+/*
+ * vomni_b200.h — C ABI of the B200-native context-parallel self-attention hot path of the
+ * Wan2.2-A14B DiT (const-max ring attention, fused adaLN + FP8 row quant, FP8 QKV projection).
+ *
+ * Plain pointers, sizes and a CUDA stream handle; no framework types. Every entry point is
+ * stream-ordered on `stream`, validates its arguments on the host and returns a vomni_status
+ * code (never aborts). Device pointers must be CUDA device (or managed) memory of the calling
+ * thread's current device. Kernels that wait on barriers bound every wait; a wait that runs out
+ * records a device-side code readable with vomni_device_status().
+ *
+ * Each entry point names the reference interface it replaces, as
+ * reecedantin/vllm-omni-neuron path:line.
+ */
+#ifndef VOMNI_B200_H
+#define VOMNI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define VOMNI_API __attribute__((visibility("default")))
+#else
+#define VOMNI_API
+#endif
+
+typedef struct CUstream_st* vomni_stream_t; /* same object as cudaStream_t / CUstream */
+
+enum vomni_status {
+  VOMNI_OK = 0,
+  VOMNI_EINVAL = 1,     /* bad argument (null pointer, unknown flag/mode)                    */
+  VOMNI_EBADSHAPE = 2,  /* unsupported shape (e.g. head_dim != 128, empty extent)            */
+  VOMNI_EALIGN = 3,     /* pointer / stride not aligned as the TMA engine requires (16 B)    */
+  VOMNI_ECUDA = 4,      /* a CUDA runtime / driver call failed                               */
+  VOMNI_ENCCL = 5,      /* NCCL failed or is unavailable                                     */
+  VOMNI_ETIMEOUT = 6,   /* a bounded device or host wait ran out                             */
+  VOMNI_ENOTSUP = 7,    /* not supported on this device (needs sm_100)                       */
+  VOMNI_EWORKSPACE = 8, /* workspace too small                                               */
+  VOMNI_ESTATE = 9      /* context misuse (wrong rank count, destroyed context, ...)         */
+};
+
+/* Device status word values (vomni_device_status): 0 = healthy; 0x1000 + site = a bounded
+ * mbarrier wait at `site` ran out. */
+#define VOMNI_DEV_TIMEOUT_BASE 0x1000
+
+/* ------------------------------------------------------------------ library */
+VOMNI_API int vomni_abi_version(void);
+VOMNI_API const char* vomni_strerror(int code);
+/* Synchronises the device, copies the status word to *code, optionally clears it. */
+VOMNI_API int vomni_device_status(int* code, int clear);
+
+/* ------------------------------------------------------------------ const-max attention
+ * Replaces the NKI kernel ring_attention_const_max_fwd
+ * (vllm_omni_neuron/kernels/nkilib/experimental/attention/ring_attention_const_max_fwd.py:958-1404)
+ * and its per-step partial _attention_const_max_partial (attention_const_max.py:69-234).
+ *
+ * Layouts (bf16): q, k, v token-major [b, s, h, d] (d must be 128). out is head-major
+ * [b, h, s, d] (the kernel's return layout, ring_attention_const_max_fwd.py:1400) or, with
+ * VOMNI_CM_OUT_DMAJOR, d-major [b, h, d, s] (the layout wan_cp_self_attention returns,
+ * wan2_2_transformer.py:836). lse (optional, fp32) is [b, h, 128, ceil(s/128)] with
+ * lse[.., r, g] for token g*128 + r (ring_attention_const_max_fwd.py:1062-1065).
+ */
+#define VOMNI_CM_ACC_IN 1     /* add the fp32 partial already in acc_o / acc_l                */
+#define VOMNI_CM_FINAL 2      /* normalise and write bf16 out (else write the fp32 partial)   */
+#define VOMNI_CM_OUT_DMAJOR 4 /* out is [b, h, d, s] instead of [b, h, s, d]                  */
+#define VOMNI_CM_LSE 8        /* also write lse = c + ln(max(sum, 1e-37))                     */
+
+/* Bytes of workspace vomni_cm_attention_local needs (norms, key max, status). */
+VOMNI_API size_t vomni_cm_workspace_bytes(int b, int s, int h, int d);
+
+/* Prologue: qn2[b*h, s] = per-token ||q||^2, kmax2[b*h] = max over this rank's tokens of ||k||^2
+ * (fp32, from the bf16 values). kmax2 is overwritten (not max-accumulated).
+ * Replaces _transpose_qk_pipelined's fused norms (ring_attention_const_max_fwd.py:424-556). */
+VOMNI_API int vomni_cm_prologue(const void* q, const void* k, int b, int s, int h, int d, float* qn2, float* kmax2,
+                      vomni_stream_t stream);
+
+/* One pass of const-max attention of all query rows against keys [k_start, k_start + n_keys) of
+ * k/v (each [b, s_kv, h, d]), with the per-row bound c_i = bf16(scale * sqrt(kmax2[bh] * qn2[bh, i])).
+ * Partial sums go to acc_o [b*h, s_q, d] / acc_l [b*h, s_q] (fp32) unless VOMNI_CM_FINAL.
+ * Replaces one ring step: _run_partial_step / _run_last_step_and_normalize
+ * (ring_attention_const_max_fwd.py:806-955). */
+VOMNI_API int vomni_cm_attend(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start, int n_keys,
+                    int h, int d, float softmax_scale, const float* qn2, const float* kmax2, float* acc_o,
+                    float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream);
+
+/* Single-rank (num_workers == 1) const-max attention: prologue + one final pass.
+ * Replaces ring_attention_const_max_fwd(num_workers=1) (ring_attention_const_max_fwd.py:1306-1327).
+ * flags: VOMNI_CM_OUT_DMAJOR / VOMNI_CM_LSE. */
+VOMNI_API int vomni_cm_attention_local(const void* q, const void* k, const void* v, void* out, float* lse, int b, int s, int h,
+                             int d, float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
+                             vomni_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOMNI_B200_H */

@@ -1,0 +1,189 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference's own code.
+
+Run in the build container, where the reference checkout is mounted (default
+``/root/reference``; override with ``VOMNI_REFERENCE``)::
+
+    python tests/golden/make_golden.py
+
+Only the reference's dependency-light torch/numpy pieces are executed (the NKI kernels
+cannot run without a Trainium toolchain):
+
+* ``adaln_quant_torch_ref`` and ``_mx_dequant`` (kernels/nkilib/experimental/norm/
+  adaln_quant_torch.py), loaded by file path;
+* ``_eager_adaln`` (diffusion/quantization/adaln_kernels.py:51-84), loaded by file path;
+* ``WanRotaryPosEmbed`` / ``apply_rotary_emb_wan`` (diffusion/layers/rope.py), by file path;
+* ``_torch_attend`` (diffusion/models/wan2_2/wan2_2_transformer.py:640-650),
+  ``DistributedRMSNorm`` (:855-893), ``_rope_rotate_half_caches``
+  (diffusion/quantization/row_mx_modules.py:51-76) and the de-interleave loaders
+  (diffusion/quantization/row_mx_loaders.py:26-71): their modules import the Neuron SDK at
+  top level, so the function definitions are extracted from the source with ``ast`` and
+  executed against plain torch.
+
+Outputs ``*.npz`` next to this script. bf16 tensors are stored as their float32 values.
+"""
+
+from __future__ import annotations
+
+import ast
+import importlib.util
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REF = Path(os.environ.get("VOMNI_REFERENCE", "/root/reference")) / "vllm_omni_neuron"
+OUT = Path(__file__).resolve().parent
+
+
+def _load_file(name: str, path: Path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _extract(path: Path, names: list[str], env: dict) -> dict:
+    """Exec only the named top-level defs/classes of a reference module against ``env``."""
+    tree = ast.parse(path.read_text())
+    body = [n for n in tree.body if isinstance(n, (ast.FunctionDef, ast.ClassDef)) and n.name in names]
+    missing = set(names) - {n.name for n in body}
+    if missing:
+        raise RuntimeError(f"{path}: missing {missing}")
+    mod = ast.Module(body=body, type_ignores=[])
+    code = compile(mod, str(path), "exec")
+    exec(code, env)
+    return {n: env[n] for n in names}
+
+
+def _bf16(t: torch.Tensor) -> np.ndarray:
+    return t.to(torch.bfloat16).float().numpy()
+
+
+def gen_adaln(rng: torch.Generator):
+    adt = _load_file("ref_adaln_quant_torch", REF / "kernels/nkilib/experimental/norm/adaln_quant_torch.py")
+    T, H = 12, 128
+    hidden = torch.randn(T, H, generator=rng).to(torch.bfloat16)
+    hidden[3, :] = 0.0  # an all-zero row exercises the 1e-6 scale floor
+    mul = (1 + 0.1 * torch.randn(H, generator=rng)).to(torch.bfloat16)
+    add = (0.1 * torch.randn(H, generator=rng)).to(torch.bfloat16)
+    residual = torch.randn(T, H, generator=rng).to(torch.bfloat16)
+    gate = 0.5 * torch.randn(H, generator=rng)
+    out = {"hidden": _bf16(hidden), "mul": _bf16(mul), "add": _bf16(add), "residual": _bf16(residual), "gate": gate.numpy()}
+    cases = []
+    for norm in ("layer_norm", "rms_norm", "none"):
+        for quant in ("none", "row", "mx"):
+            for res_mode in ("plain", "residual", "gated"):
+                for ocp in ((True, False) if quant == "row" else (True,)):
+                    kw = dict(norm_type=norm, quant=quant, eps=1e-6, ocp=ocp)
+                    if res_mode != "plain":
+                        kw["residual"] = residual
+                    if res_mode == "gated":
+                        kw["gate"] = gate
+                    r = adt.adaln_quant_torch_ref(hidden, mul, add, **kw)
+                    key = f"{norm}|{quant}|{res_mode}|{int(ocp)}"
+                    cases.append(key)
+                    for f in ("y", "quant", "dequant_scale", "dequant"):
+                        if r[f] is not None:
+                            out[f"{key}|{f}"] = np.asarray(r[f], np.float32)
+                    if r["residual_out"] is not None:
+                        out[f"{res_mode}|residual_out"] = np.asarray(r["residual_out"], np.float32)
+    out["cases"] = np.array(cases)
+    np.savez_compressed(OUT / "adaln_ref.npz", **out)
+
+
+def gen_eager_adaln(rng: torch.Generator):
+    adk = _load_file("ref_adaln_kernels", REF / "diffusion/quantization/adaln_kernels.py")
+    B, S, H = 2, 24, 128
+    hidden = torch.randn(B, S, H, generator=rng).to(torch.bfloat16)
+    mul = (1 + 0.1 * torch.randn(B, 1, H, generator=rng)).to(torch.bfloat16)
+    add = (0.1 * torch.randn(B, 1, H, generator=rng)).to(torch.bfloat16)
+    residual = torch.randn(B, S, H, generator=rng).to(torch.bfloat16)
+    gate = 0.5 * torch.randn(B, 1, H, generator=rng)
+    out = {"hidden": _bf16(hidden), "mul": _bf16(mul), "add": _bf16(add), "residual": _bf16(residual), "gate": gate.numpy()}
+    for norm in ("layer_norm", "rms_norm", "none"):
+        o = adk._eager_adaln(hidden, mul, add, eps=1e-6, norm_type=norm, quant="none")
+        out[f"{norm}|plain|out"] = _bf16(o)
+        ro, o = adk._eager_adaln(hidden, mul, add, eps=1e-6, norm_type=norm, quant="none", residual=residual, gate=gate)
+        out[f"{norm}|gated|residual_out"] = _bf16(ro)
+        out[f"{norm}|gated|out"] = _bf16(o)
+    np.savez_compressed(OUT / "eager_adaln.npz", **out)
+
+
+def gen_attention(rng: torch.Generator):
+    wt = REF / "diffusion/models/wan2_2/wan2_2_transformer.py"
+    fns = _extract(wt, ["_torch_attend"], {"torch": torch})
+    out = {}
+    for tag, (B, N, S, Sk) in {"a": (1, 2, 96, 96), "b": (2, 1, 130, 140)}.items():
+        q = (0.5 * torch.randn(B, N, S, 128, generator=rng)).to(torch.bfloat16)
+        k = (0.5 * torch.randn(B, N, Sk, 128, generator=rng)).to(torch.bfloat16)
+        v = (0.5 * torch.randn(B, N, Sk, 128, generator=rng)).to(torch.bfloat16)
+        scale = 1.0 / 128 ** 0.5
+        o = fns["_torch_attend"](q, k, v, scale)
+        out.update({f"{tag}|q": _bf16(q), f"{tag}|k": _bf16(k), f"{tag}|v": _bf16(v), f"{tag}|scale": np.float32(scale), f"{tag}|o": _bf16(o)})
+    np.savez_compressed(OUT / "torch_attend.npz", **out)
+
+
+def gen_rope_norm(rng: torch.Generator):
+    rope = _load_file("ref_rope", REF / "diffusion/layers/rope.py")
+    emb = rope.WanRotaryPosEmbed(128, (1, 2, 2), 1024)
+    latent = torch.zeros(1, 16, 3, 6, 8)
+    cos, sin = emb(latent)
+    S = cos.shape[1]
+    x = torch.randn(1, S, 2, 128, generator=rng).to(torch.bfloat16)
+    xr = rope.apply_rotary_emb_wan(x, cos, sin)
+    rmm = _extract(REF / "diffusion/quantization/row_mx_modules.py", ["_rope_rotate_half_caches"], {"torch": torch})
+    cos_rh, sin_rh = rmm["_rope_rotate_half_caches"]((cos, sin), 1, 128)
+    rml = _extract(
+        REF / "diffusion/quantization/row_mx_loaders.py",
+        ["deinterleave_perm", "_deinterleave_qk_columns", "deinterleave_gamma_row"],
+        {"torch": torch},
+    )
+    w = torch.randn(4, 3 * 256, generator=rng)
+    wd = rml["_deinterleave_qk_columns"](w, 256, 256, 128)
+    gamma = torch.randn(256, generator=rng)
+    gd = rml["deinterleave_gamma_row"](gamma, 128)
+
+    # DistributedRMSNorm at TP=1: the class with its process-group helpers stubbed to TP=1.
+    env = {
+        "torch": torch,
+        "nn": torch.nn,
+        "dist": None,
+        "get_tensor_model_parallel_world_size": lambda: 1,
+        "get_tp_group": lambda: types.SimpleNamespace(device_group=None),
+        "set_weight_loader": lambda *a, **k: None,
+        "sharding_weight_loader": lambda *a, **k: None,
+    }
+    cls = _extract(REF / "diffusion/models/wan2_2/wan2_2_transformer.py", ["DistributedRMSNorm"], env)["DistributedRMSNorm"]
+    norm = cls(256, eps=1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(256, generator=rng))
+    xn = torch.randn(1, S, 256, generator=rng).to(torch.bfloat16)
+    with torch.no_grad():
+        yn = norm(xn)
+    np.savez_compressed(
+        OUT / "rope_norm.npz",
+        cos=cos.numpy(), sin=sin.numpy(), x=_bf16(x), x_rope=_bf16(xr),
+        cos_rh=cos_rh.numpy(), sin_rh=sin_rh.numpy(),
+        w=w.numpy(), w_deint=wd.numpy(), gamma=gamma.numpy(), gamma_deint=gd.numpy(),
+        norm_w=norm.weight.detach().numpy(), norm_x=_bf16(xn), norm_y=_bf16(yn),
+        latent_fhw=np.array([3, 6, 8]),
+    )
+
+
+def main():
+    if not REF.exists():
+        sys.exit(f"reference checkout not found at {REF}")
+    rng = torch.Generator().manual_seed(20261201)
+    gen_adaln(rng)
+    gen_eager_adaln(rng)
+    gen_attention(rng)
+    gen_rope_norm(rng)
+    for p in sorted(OUT.glob("*.npz")):
+        print(p.name, p.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

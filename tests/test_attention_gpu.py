@@ -1,0 +1,164 @@
+"""GPU parity of the const-max attention kernels against the CPU oracle (B200 only)."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oat
+
+pytestmark = pytest.mark.gpu
+
+TOL_COS = 0.9999  # north-star tolerance for bf16 attention vs an fp32 reference
+TOL_ABS = 2e-2
+
+
+def _f32(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _cmp(got, ref, what=""):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    assert np.isfinite(got).all(), what
+    cos = (got * ref).sum() / math.sqrt((got * got).sum() * (ref * ref).sum() + 1e-300)
+    mx = np.abs(got - ref).max()
+    assert cos >= TOL_COS and mx <= TOL_ABS, f"{what}: cos={cos:.6f} maxabs={mx:.4g}"
+
+
+def _rand_qkv(b, s, h, seed, dev, scale=0.5):
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda: (torch.randn(b, s, h, 128, generator=g) * scale).to(torch.bfloat16)
+    return [x.to(dev) for x in (mk(), mk(), mk())]
+
+
+@pytest.mark.parametrize(
+    "b,s,h",
+    [(1, 128, 1), (1, 256, 2), (2, 130, 3), (1, 127, 2), (1, 1, 1), (1, 1000, 2), (1, 4095, 1)],
+)
+def test_local_vs_oracle(pkg, dev, b, s, h):
+    q, k, v = _rand_qkv(b, s, h, 1000 + s + h, dev)
+    o = pkg.ring_attention_const_max_fwd(q, k, v)
+    torch.cuda.synchronize()
+    assert tuple(o.shape) == (b, h, s, 128)
+    qn, kn, vn = _f32(q), _f32(k), _f32(v)
+    ref_exact = oat.torch_attend(*(np.transpose(x, (0, 2, 1, 3)) for x in (qn, kn, vn)), 1 / math.sqrt(128))
+    _cmp(_f32(o), ref_exact, "vs exact")
+    ref_cm = oat.const_max_ring_attention([qn], [kn], [vn])[0]
+    _cmp(_f32(o), ref_cm, "vs const-max oracle")
+    from importlib import import_module
+
+    assert import_module("vllm-omni-neuron_b200._lib").device_status() == 0
+
+
+def test_golden_torch_attend(pkg, dev, golden):
+    """On the inputs of the reference's own _torch_attend golden vectors (S_q == S_k case)."""
+    g = golden("torch_attend.npz")
+    q, k, v = (torch.from_numpy(np.ascontiguousarray(np.transpose(g[f"a|{n}"], (0, 2, 1, 3)))).to(torch.bfloat16).to(dev) for n in "qkv")
+    o = pkg.ring_attention_const_max_fwd(q, k, v, softmax_scale=float(g["a|scale"]))
+    _cmp(_f32(o), g["a|o"], "golden a")
+
+
+def test_dmajor_and_lse(pkg, dev):
+    b, s, h = 1, 300, 2
+    q, k, v = _rand_qkv(b, s, h, 7, dev)
+    o_bhsd, lse = pkg.ring_attention_const_max_fwd(q, k, v, training=True)
+    o_bhds = pkg.wan_cp_self_attention(q, k, v, 1 / math.sqrt(128), 1, None, None)
+    torch.cuda.synchronize()
+    assert tuple(o_bhds.shape) == (b, h, 128, s)
+    assert torch.equal(o_bhds, o_bhsd.transpose(2, 3).contiguous())
+    qn, kn, vn = _f32(q), _f32(k), _f32(v)
+    _, ref_lse = oat.const_max_ring_attention([qn], [kn], [vn], training=True)
+    got = _f32(lse)
+    ref = ref_lse[0]
+    # LSE only defined on real rows; pad rows of the last group stay 0 (zero-initialised).
+    assert np.abs(got - ref).max() < 2e-2
+    # lse is exact softmax log-normaliser: compare with log-sum-exp of fp32 scores
+    sc = np.einsum("bshd,bthd->bhst", qn, kn) / math.sqrt(128)
+    lse_exact = np.log(np.exp(sc - sc.max(-1, keepdims=True)).sum(-1)) + sc.max(-1)
+    for gi in range(-(-s // 128)):
+        rows = min(128, s - gi * 128)
+        assert np.abs(got[:, :, :rows, gi] - lse_exact[:, :, gi * 128:gi * 128 + rows]).max() < 5e-2
+
+
+@pytest.mark.parametrize("n", [2, 3, 4])
+def test_ring_steps_emulated(pkg, dev, n):
+    """The ring's per-step path on one GPU: prologue per rank, global key max, then one
+    vomni_cm_attend pass per ring step in ring order (step s consumes rank (r-s) mod n's block),
+    accumulating in fp32 and normalising on the last step. Checked against the oracle ring."""
+    from importlib import import_module
+
+    lib = import_module("vllm-omni-neuron_b200._lib")
+    L = lib.load()
+    b, s, h = 1, 200, 2
+    qs, ks, vs = [], [], []
+    for r in range(n):
+        q, k, v = _rand_qkv(b, s, h, 50 + r, dev)
+        qs.append(q), ks.append(k), vs.append(v)
+    st = torch.cuda.current_stream().cuda_stream
+    qn2 = [torch.empty(b * h, s, dtype=torch.float32, device=dev) for _ in range(n)]
+    km = [torch.empty(b * h, dtype=torch.float32, device=dev) for _ in range(n)]
+    for r in range(n):
+        lib.check(L.vomni_cm_prologue(qs[r].data_ptr(), ks[r].data_ptr(), b, s, h, 128, qn2[r].data_ptr(), km[r].data_ptr(), st), "prologue")
+    kmax = torch.stack(km).amax(0)
+    outs = []
+    for r in range(n):
+        acc_o = torch.empty(b * h, s, 128, dtype=torch.float32, device=dev)
+        acc_l = torch.empty(b * h, s, dtype=torch.float32, device=dev)
+        out = torch.empty(b, h, s, 128, dtype=torch.bfloat16, device=dev)
+        for step in range(n):
+            src = (r - step) % n
+            flags = (lib.CM_ACC_IN if step > 0 else 0) | (lib.CM_FINAL if step == n - 1 else 0)
+            lib.check(
+                L.vomni_cm_attend(
+                    qs[r].data_ptr(), ks[src].data_ptr(), vs[src].data_ptr(), b, s, s, 0, s, h, 128, 1 / math.sqrt(128),
+                    qn2[r].data_ptr(), kmax.data_ptr(), acc_o.data_ptr(), acc_l.data_ptr(), flags, out.data_ptr(), None, st,
+                ),
+                "attend",
+            )
+        outs.append(out)
+    torch.cuda.synchronize()
+    ref = oat.const_max_ring_attention([_f32(x) for x in qs], [_f32(x) for x in ks], [_f32(x) for x in vs])
+    exact = oat.wan_cp_self_attention_oracle([_f32(x) for x in qs], [_f32(x) for x in ks], [_f32(x) for x in vs], 1 / math.sqrt(128))
+    for r in range(n):
+        _cmp(_f32(outs[r]), ref[r], f"rank {r} vs oracle ring")
+        _cmp(_f32(outs[r]).transpose(0, 1, 3, 2), exact[r], f"rank {r} vs exact")
+    assert lib.device_status() == 0
+
+
+def test_key_subrange_masking(pkg, dev):
+    """A pass over keys [k_start, k_start+n_keys) of a longer K/V must ignore the keys outside."""
+    from importlib import import_module
+
+    lib = import_module("vllm-omni-neuron_b200._lib")
+    L = lib.load()
+    b, s, h, skv = 1, 160, 1, 700
+    q, _, _ = _rand_qkv(b, s, h, 3, dev)
+    _, k, v = _rand_qkv(b, skv, h, 4, dev)
+    k0, nk = 150, 301
+    st = torch.cuda.current_stream().cuda_stream
+    qn2 = torch.empty(b * h, s, dtype=torch.float32, device=dev)
+    km = torch.empty(b * h, dtype=torch.float32, device=dev)
+    ksub = k[:, k0:k0 + nk].contiguous()
+    vsub = v[:, k0:k0 + nk].contiguous()
+    qpad = torch.zeros(b, nk, h, 128, dtype=torch.bfloat16, device=dev)
+    qpad[:, :s] = q
+    # norms of q (first s rows) and of the key sub-range
+    lib.check(L.vomni_cm_prologue(qpad.data_ptr(), ksub.data_ptr(), b, nk, h, 128, torch.empty(b * h, nk, device=dev).data_ptr(), km.data_ptr(), st), "p1")
+    lib.check(L.vomni_cm_prologue(q.data_ptr(), q.data_ptr(), b, s, h, 128, qn2.data_ptr(), torch.empty(b * h, device=dev).data_ptr(), st), "p2")
+    out = torch.empty(b, h, s, 128, dtype=torch.bfloat16, device=dev)
+    lib.check(L.vomni_cm_attend(q.data_ptr(), k.data_ptr(), v.data_ptr(), b, s, skv, k0, nk, h, 128, 1 / math.sqrt(128), qn2.data_ptr(), km.data_ptr(), None, None, lib.CM_FINAL, out.data_ptr(), None, st), "attend")
+    torch.cuda.synchronize()
+    ref = oat.torch_attend(np.transpose(_f32(q), (0, 2, 1, 3)), np.transpose(_f32(ksub), (0, 2, 1, 3)), np.transpose(_f32(vsub), (0, 2, 1, 3)), 1 / math.sqrt(128))
+    _cmp(_f32(out), ref, "subrange")
+    assert lib.device_status() == 0
+
+
+def test_errors(pkg, dev):
+    q, k, v = _rand_qkv(1, 64, 1, 0, dev)
+    with pytest.raises(AssertionError):
+        pkg.ring_attention_const_max_fwd(q[..., :64].contiguous(), k[..., :64].contiguous(), v[..., :64].contiguous())
+    with pytest.raises(TypeError):
+        pkg.ring_attention_const_max_fwd(q.float(), k, v)

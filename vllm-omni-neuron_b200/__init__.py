@@ -1,0 +1,22 @@
+"""B200-native (sm_100a) context-parallel self-attention hot path of the Wan2.2-A14B DiT.
+
+Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call API:
+
+* :func:`ring_attention_const_max_fwd` — const-max ring attention (the NKI kernel's API)
+* :func:`wan_cp_self_attention` — the Wan attention processor core
+* :func:`adaln_modulate` — fused gated-residual + (Layer|RMS)Norm + modulation + FP8 row quant
+* :func:`row_mx_qkv_proj` — FP8 QKV projection with across-heads RMS norm + rotate-half RoPE
+
+Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``) built by
+:func:`build`.
+"""
+
+from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
+from .build import build
+
+__all__ = [
+    "attention_local",
+    "build",
+    "ring_attention_const_max_fwd",
+    "wan_cp_self_attention",
+]

@@ -1,0 +1,136 @@
+"""Const-max (ring) attention: the reference's kernel-call API and attention processor on B200.
+
+* :func:`ring_attention_const_max_fwd` keeps the signature and return contract of the NKI kernel
+  (vllm_omni_neuron/kernels/nkilib/experimental/attention/ring_attention_const_max_fwd.py:958-1017):
+  token-major ``q, k, v [b, S_loc, h, 128]`` bf16 in, head-major ``o [b, h, S_loc, 128]`` out
+  (plus ``lse [b, h, 128, ceil(S_loc/128)]`` fp32 when ``training``); ``softmax_scale`` defaults
+  to ``1/sqrt(d)``; ``kv_prefetch_depth`` is clamped to ``[1, num_workers-1]``; shape contract
+  violations raise ``AssertionError`` as the kernel's ``kernel_assert`` does (:1019-1031).
+* :func:`wan_cp_self_attention` keeps the attention-processor signature
+  (vllm_omni_neuron/diffusion/models/wan2_2/wan2_2_transformer.py:806-847) and returns the d-major
+  ``[B, N, D, S_loc]`` layout directly from the kernel epilogue (the reference transposes after the
+  kernel, :836).
+
+All compute runs in ``libvomni_b200.so`` (sm_100a). There is no fallback path: a missing library or
+a non-sm_100 device raises.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_HEAD_DIM = 128
+
+
+def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    assert q.dim() == 4 and k.dim() == 4 and v.dim() == 4, "q, k, v must be token-major [b, seqlen, h, d]"
+    b, s, h, d = q.shape
+    assert k.shape[2] == h, "expects q_heads == kv_heads, broadcast before calling"
+    assert d == _HEAD_DIM, f"head_dim must be 128, got {d}"
+    assert tuple(k.shape) == (b, s, h, d) and tuple(v.shape) == (b, s, h, d), (
+        f"q and k must be token-major [b, seqlen, h, d]; got q={tuple(q.shape)}, k={tuple(k.shape)}"
+    )
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor (the B200 kernel has no CPU path)")
+    return b, s, h, d
+
+
+def _stream_ptr(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def attention_local(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    softmax_scale: float | None = None,
+    *,
+    out_layout: str = "bhsd",
+    training: bool = False,
+):
+    """Single-rank const-max attention (``num_workers == 1``): prologue norms + one final pass.
+
+    ``out_layout``: ``"bhsd"`` (kernel layout) or ``"bhds"`` (d-major, the attention-processor
+    layout). Returns ``o`` or ``(o, lse)``.
+    """
+    b, s, h, d = _check_qkv(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
+    lib = _lib.load()
+    flags = 0
+    if out_layout == "bhds":
+        flags |= _lib.CM_OUT_DMAJOR
+        out = torch.empty((b, h, d, s), dtype=torch.bfloat16, device=q.device)
+    elif out_layout == "bhsd":
+        out = torch.empty((b, h, s, d), dtype=torch.bfloat16, device=q.device)
+    else:
+        raise ValueError(f"unknown out_layout {out_layout!r}")
+    lse = None
+    if training:
+        flags |= _lib.CM_LSE
+        lse = torch.zeros((b, h, 128, -(-s // 128)), dtype=torch.float32, device=q.device)
+    ws_bytes = lib.vomni_cm_workspace_bytes(b, s, h, d)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    rc = lib.vomni_cm_attention_local(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if lse is not None else None,
+        b, s, h, d, scale, flags, ws.data_ptr(), ws_bytes, _stream_ptr(q.device),
+    )
+    _lib.check(rc, "vomni_cm_attention_local")
+    return (out, lse) if training else out
+
+
+def ring_attention_const_max_fwd(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    replica_groups: tuple | None = None,
+    num_workers: int = 1,
+    softmax_scale: float | None = None,
+    training: bool = False,
+    lse_dtype: torch.dtype = torch.float32,
+    kv_prefetch_depth: int = 2,
+    *,
+    group=None,
+    out_layout: str = "bhsd",
+):
+    """Fixed-max ring attention forward (non-causal); see the module docstring for the contract.
+
+    ``group`` (B200 addition): the ``torch.distributed`` process group of this rank's ring when
+    ``num_workers > 1``; defaults to the group matching ``replica_groups`` (built once per ring).
+    """
+    _check_qkv(q, k, v)
+    if num_workers <= 1:
+        res = attention_local(q, k, v, softmax_scale, out_layout=out_layout, training=training)
+    else:
+        from .ring import ring_attention
+
+        res = ring_attention(
+            q, k, v, replica_groups=replica_groups, num_workers=num_workers, softmax_scale=softmax_scale,
+            training=training, kv_prefetch_depth=kv_prefetch_depth, group=group, out_layout=out_layout,
+        )
+    if training:
+        o, lse = res
+        return o, lse.to(lse_dtype)
+    return res
+
+
+def wan_cp_self_attention(query, key, value, scale, cp_size, cp_group, cp_replica_groups):
+    """Context-parallel self-attention core (wan2_2_transformer.py:806-847).
+
+    ``query/key/value``: token-major ``[B, local_S, N, D]`` bf16. Returns d-major ``[B, N, D, local_S]``.
+    ``cp_group``: a ``torch.distributed`` ProcessGroup, or an object exposing one as
+    ``device_group`` (vLLM's GroupCoordinator), or None when ``cp_size == 1``. The ring kernel runs at
+    every ``cp_size`` (``num_workers=1`` included); there is no all-gather fallback.
+    """
+    group = getattr(cp_group, "device_group", cp_group)
+    return ring_attention_const_max_fwd(
+        query, key, value, replica_groups=cp_replica_groups, num_workers=int(cp_size), softmax_scale=scale,
+        group=group, out_layout="bhds",
+    )

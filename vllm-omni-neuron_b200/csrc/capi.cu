@@ -1,0 +1,148 @@
+// Library-level C ABI: version, error strings, the device status word, device checks and TMA
+// descriptor encoding shared by the kernel translation units.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "host_util.h"
+
+// One status word per device that loads the library; bounded device waits write their error
+// code here (first error wins) and vomni_device_status() reads / clears it.
+__device__ int g_vomni_status;
+
+namespace vomni {
+
+namespace {
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {};
+int g_num_sms[kMaxDevices] = {};
+int g_is_sm100[kMaxDevices] = {};  // 0 unknown, 1 yes, -1 no
+std::mutex g_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+}  // namespace
+
+void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = e; }
+
+int num_sms() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (!g_num_sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_num_sms[dev] = n;
+  }
+  return g_num_sms[dev];
+}
+
+int require_sm100() {
+  const int dev = current_device();
+  if (dev < 0) return VOMNI_ECUDA;
+  if (dev < kMaxDevices && g_is_sm100[dev]) return g_is_sm100[dev] > 0 ? VOMNI_OK : VOMNI_ENOTSUP;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return VOMNI_ECUDA;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return VOMNI_ECUDA;
+  const bool ok = (major == 10 && minor == 0);
+  if (dev < kMaxDevices) g_is_sm100[dev] = ok ? 1 : -1;
+  return ok ? VOMNI_OK : VOMNI_ENOTSUP;
+}
+
+int* device_status_ptr() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (!g_status_ptr[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_status_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_vomni_status) != cudaSuccess) return nullptr;
+      g_status_ptr[dev] = static_cast<int*>(p);
+    }
+  }
+  return g_status_ptr[dev];
+}
+
+static int get_encoder() {
+  if (g_encode) return VOMNI_OK;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_encode) return VOMNI_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn)
+    return VOMNI_ECUDA;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return VOMNI_OK;
+}
+
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
+                      uint32_t box1) {
+  int rc = get_encoder();
+  if (rc) return rc;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return VOMNI_EALIGN;
+  if ((dim0 * 2) % 16) return VOMNI_EALIGN;
+  cuuint64_t dims[3] = {dim0, dim1, dim2};
+  cuuint64_t strides[2] = {dim0 * 2, dim0 * dim1 * 2};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? VOMNI_OK : VOMNI_ECUDA;
+}
+
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                 uint64_t pitch_bytes, uint32_t box0, uint32_t box1) {
+  int rc = get_encoder();
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch_bytes % 16)) return VOMNI_EALIGN;
+  cuuint64_t dims[2] = {dim0, dim1};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box0, box1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? VOMNI_OK : VOMNI_ECUDA;
+}
+
+}  // namespace vomni
+
+extern "C" int vomni_abi_version(void) { return 1; }
+
+extern "C" const char* vomni_strerror(int code) {
+  switch (code) {
+    case VOMNI_OK: return "ok";
+    case VOMNI_EINVAL: return "invalid argument";
+    case VOMNI_EBADSHAPE: return "unsupported shape";
+    case VOMNI_EALIGN: return "pointer or stride not 16-byte aligned";
+    case VOMNI_ECUDA: {
+      static thread_local char buf[160];
+      snprintf(buf, sizeof(buf), "CUDA error: %s", cudaGetErrorString(vomni::g_last_cuda_error));
+      return buf;
+    }
+    case VOMNI_ENCCL: return "NCCL error";
+    case VOMNI_ETIMEOUT: return "bounded wait timed out";
+    case VOMNI_ENOTSUP: return "not supported on this device (needs sm_100)";
+    case VOMNI_EWORKSPACE: return "workspace too small";
+    case VOMNI_ESTATE: return "invalid context state";
+    default: return "unknown error";
+  }
+}
+
+extern "C" int vomni_device_status(int* code, int clear) {
+  if (!code) return VOMNI_EINVAL;
+  int* p = vomni::device_status_ptr();
+  if (!p) return VOMNI_ECUDA;
+  VOMNI_CUDA_TRY(cudaDeviceSynchronize());
+  VOMNI_CUDA_TRY(cudaMemcpy(code, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear) VOMNI_CUDA_TRY(cudaMemset(p, 0, sizeof(int)));
+  return VOMNI_OK;
+}

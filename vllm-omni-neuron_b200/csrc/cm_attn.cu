@@ -1,0 +1,443 @@
+// Const-max attention for sm_100a: prologue norms + a warp-specialised tcgen05/TMEM attention pass.
+//
+// Algorithm (reference: vllm_omni_neuron/kernels/nkilib/experimental/attention/
+// ring_attention_const_max_fwd.py and attention_const_max.py): every query row i carries a fixed
+// softmax bound c_i = scale * ||q_i|| * max_j ||k_j|| (Cauchy-Schwarz, so scale*q_i.k_j - c_i <= 0),
+// computed once from a prologue. With a fixed bound there is no running max and no rescaling:
+//     O_i += sum_j exp(scale*q_i.k_j - c_i) v_j,   l_i += sum_j exp(...)
+// and partial results of different key ranges (ring steps) combine by plain addition; one final
+// normalise o_i = O_i / max(l_i, 1e-37).
+//
+// Kernel layout (one CTA = one 128-row query tile of one (batch, head)):
+//   warp 0      TMA producer: Q once, then K/V 128-key tiles into a 2-stage ring (no multicast)
+//   warp 1      TMEM owner + MMA issuer (one elected lane): S = Q K^T (SS form), O += P V (TS form,
+//               P read straight from TMEM)
+//   warps 2..5  softmax: one query row per thread (TMEM lane), P = exp2(S*scale*log2e - c*log2e)
+//               written back to TMEM as bf16, then the epilogue (normalise / partial write)
+// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace vomni {
+namespace cm {
+
+constexpr int kTile = 128;  // query rows per CTA and keys per tile
+constexpr int kD = 128;     // head dim (the reference asserts 128, ring_attention_const_max_fwd.py:1026)
+constexpr int kThreads = 192;
+constexpr uint32_t kTileBytes = kTile * kD * 2;  // 32 KB: one bf16 [128 x 128] tile
+constexpr uint32_t kHalfBytes = kTileBytes / 2;  // 16 KB: one [128 x 64] swizzled half
+
+// smem map (offsets from a 1024-aligned base)
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemK = kSmemQ + kTileBytes;       // 2 stages
+constexpr uint32_t kSmemV = kSmemK + 2 * kTileBytes;   // 2 stages
+constexpr uint32_t kSmemBar = kSmemV + 2 * kTileBytes;  // barriers + scalars
+constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + alignment slack
+
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 11, P_EMPTY = 13, O_FULL = 15, NBAR = 16 };
+
+constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
+constexpr uint32_t kIdescQK = idesc_bf16(128, 128, false);
+constexpr uint32_t kIdescPV = idesc_bf16(128, 128, true);
+
+struct Params {
+  int s_q;          // query rows per (batch, head)
+  int heads;        // h
+  int n_keys;       // keys in this pass
+  int k_start;      // first key row in the K/V maps
+  float scale_log2;  // softmax_scale * log2(e)
+  float scale;      // softmax_scale
+  const float* qn2;    // [b*h, s_q]
+  const float* kmax2;  // [b*h]
+  float* acc_o;        // [b*h, s_q, 128]
+  float* acc_l;        // [b*h, s_q]
+  void* out;           // bf16
+  float* lse;          // [b*h, 128, ceil(s_q/128)]
+  int flags;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    cm_attend_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + NBAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + NBAR * 8 + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q_tile = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.heads;
+  const int h = bh % p.heads;
+  const int n_tiles = (p.n_keys + kTile - 1) / kTile;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[Q_FULL], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[K_FULL + i], 1);
+      mbar_init(&bars[K_EMPTY + i], 1);
+      mbar_init(&bars[V_FULL + i], 1);
+      mbar_init(&bars[V_EMPTY + i], 1);
+      mbar_init(&bars[S_FULL + i], 1);
+      mbar_init(&bars[P_FULL + i], 128);
+      mbar_init(&bars[P_EMPTY + i], 1);
+    }
+    mbar_init(&bars[O_FULL], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_base_slot;
+
+  uint8_t* sQ = smem + kSmemQ;
+  uint8_t* sK = smem + kSmemK;
+  uint8_t* sV = smem + kSmemV;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int q_row = q_tile * kTile;
+      const int x0 = h * kD;
+      mbar_expect_tx(&bars[Q_FULL], kTileBytes);
+      tma_load_3d(&tmQ, &bars[Q_FULL], sQ, x0, q_row, b);
+      tma_load_3d(&tmQ, &bars[Q_FULL], sQ + kHalfBytes, x0 + 64, q_row, b);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int k_row = p.k_start + j * kTile;
+        if (j >= 2 && !mbar_wait(&bars[K_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 1)) break;
+        mbar_expect_tx(&bars[K_FULL + st], kTileBytes);
+        tma_load_3d(&tmK, &bars[K_FULL + st], sK + st * kTileBytes, x0, k_row, b);
+        tma_load_3d(&tmK, &bars[K_FULL + st], sK + st * kTileBytes + kHalfBytes, x0 + 64, k_row, b);
+        if (j >= 2 && !mbar_wait(&bars[V_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 2)) break;
+        mbar_expect_tx(&bars[V_FULL + st], kTileBytes);
+        tma_load_3d(&tmV, &bars[V_FULL + st], sV + st * kTileBytes, x0, k_row, b);
+        tma_load_3d(&tmV, &bars[V_FULL + st], sV + st * kTileBytes + kHalfBytes, x0 + 64, k_row, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t k_addr = smem_u32(sK);
+      const uint32_t v_addr = smem_u32(sV);
+      bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 3);
+      tc_fence_after();
+      for (int j = 0; ok && j <= n_tiles; ++j) {
+        if (j < n_tiles) {
+          const int st = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&bars[K_FULL + st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4)) break;
+          tc_fence_after();
+          const uint32_t d_s = tbase + kColS + st * 128;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            // K-major SW128: 16-element K step = +32 B inside a 128-B row; second 64-wide half at +16 KB.
+            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+            const uint64_t a = make_sdesc(q_addr + off, 16, 1024, kLayoutSW128);
+            const uint64_t bd = make_sdesc(k_addr + st * kTileBytes + off, 16, 1024, kLayoutSW128);
+            mma_f16_ss(d_s, a, bd, kIdescQK, kk > 0);
+          }
+          tc_commit(&bars[S_FULL + st]);
+          tc_commit(&bars[K_EMPTY + st]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          const int bb = jj & 1;
+          const uint32_t ph = (jj >> 1) & 1;
+          if (!mbar_wait(&bars[P_FULL + bb], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) break;
+          if (!mbar_wait(&bars[V_FULL + bb], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            // V is [keys][d] = MN-major B: 16 keys = two 8-row groups = +2048 B; d halves 16 KB apart (LBO).
+            const uint64_t bd = make_sdesc(v_addr + bb * kTileBytes + kk * 2048, kHalfBytes, 1024, kLayoutSW128);
+            mma_f16_ts(tbase + kColO, tbase + kColP + bb * 64 + kk * 8, bd, kIdescPV, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&bars[V_EMPTY + bb]);
+          tc_commit(&bars[P_EMPTY + bb]);
+        }
+      }
+      tc_commit(&bars[O_FULL]);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (warps 2..5)
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const int grow = q_tile * kTile + row;
+    const bool row_ok = grow < p.s_q;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const size_t rowidx = static_cast<size_t>(bh) * p.s_q + grow;
+    float c = 0.f;
+    if (row_ok) {
+      // c_i = scale * sqrt(kmax2 * ||q_i||^2), held in bf16 like the reference's c_row
+      // (ring_attention_const_max_fwd.py:585-591).
+      const float c32 = p.scale * sqrtf(p.kmax2[bh] * p.qn2[rowidx]);
+      c = __bfloat162float(__float2bfloat16_rn(c32));
+    }
+    const float neg_c2 = -c * 1.4426950408889634f;
+    float rowsum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int bb = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!mbar_wait(&bars[S_FULL + bb], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+      if (j >= 2 && !mbar_wait(&bars[P_EMPTY + bb], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 8)) { ok = false; break; }
+      tc_fence_after();
+      const int valid = p.n_keys - j * kTile;  // keys of this tile inside the pass's range
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t s[32];
+        tmem_ld32(tbase + lane_addr + kColS + bb * 128 + ch * 32, s);
+        tmem_ld_wait(s);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * i]), p.scale_log2, neg_c2));
+          float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * i + 1]), p.scale_log2, neg_c2));
+          if (valid < kTile) {
+            if (ch * 32 + 2 * i >= valid) p0 = 0.f;
+            if (ch * 32 + 2 * i + 1 >= valid) p1 = 0.f;
+          }
+          rowsum += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tbase + lane_addr + kColP + bb * 64 + ch * 16, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[P_FULL + bb]);
+    }
+    // ---------------------------------------------------------- epilogue
+    if (ok && mbar_wait(&bars[O_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) {
+      tc_fence_after();
+      const bool acc_in = p.flags & VOMNI_CM_ACC_IN;
+      const bool final_pass = p.flags & VOMNI_CM_FINAL;
+      float l = rowsum;
+      if (acc_in && row_ok) l += p.acc_l[rowidx];
+      const float inv = 1.f / fmaxf(l, 1e-37f);
+      float* acc_row = p.acc_o ? p.acc_o + rowidx * kD : nullptr;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t o[32];
+        tmem_ld32(tbase + lane_addr + kColO + ch * 32, o);
+        tmem_ld_wait(o);
+        if (!row_ok) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]);
+        if (acc_in) {
+          const float4* src = reinterpret_cast<const float4*>(acc_row + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 a = src[i];
+            v[4 * i] += a.x; v[4 * i + 1] += a.y; v[4 * i + 2] += a.z; v[4 * i + 3] += a.w;
+          }
+        }
+        if (!final_pass) {
+          float4* dst = reinterpret_cast<float4*>(acc_row + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else if (p.flags & VOMNI_CM_OUT_DMAJOR) {
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(bh) * kD * p.s_q;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) out[static_cast<size_t>(ch * 32 + i) * p.s_q + grow] = __float2bfloat16_rn(v[i] * inv);
+        } else {
+          uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + rowidx * kD + ch * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 w;
+            w.x = pack_bf16x2(v[8 * i] * inv, v[8 * i + 1] * inv);
+            w.y = pack_bf16x2(v[8 * i + 2] * inv, v[8 * i + 3] * inv);
+            w.z = pack_bf16x2(v[8 * i + 4] * inv, v[8 * i + 5] * inv);
+            w.w = pack_bf16x2(v[8 * i + 6] * inv, v[8 * i + 7] * inv);
+            out[i] = w;
+          }
+        }
+      }
+      if (row_ok) {
+        if (!final_pass) {
+          p.acc_l[rowidx] = l;
+        } else if (p.flags & VOMNI_CM_LSE) {
+          const int groups = (p.s_q + 127) / 128;
+          p.lse[(static_cast<size_t>(bh) * 128 + (grow & 127)) * groups + (grow >> 7)] = c + logf(fmaxf(l, 1e-37f));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ---------------------------------------------------------------- prologue norms
+// One half-warp per (batch, token, head) row of 128 bf16: per-token ||q||^2 to qn2, and the
+// per-head max of ||k||^2 folded through shared memory into kmax2 (atomicMax on the float bits,
+// valid because sums of squares are non-negative).
+__global__ void cm_norms_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, int b, int s,
+                                int h, float* __restrict__ qn2, unsigned int* __restrict__ kmax2_bits) {
+  extern __shared__ unsigned int smax[];  // [b*h]
+  const int bhn = b * h;
+  for (int i = threadIdx.x; i < bhn; i += blockDim.x) smax[i] = 0u;
+  __syncthreads();
+  const long long rows = static_cast<long long>(b) * s * h;
+  const int half = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int sub = threadIdx.x & 15;
+  const unsigned hmask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
+  const int halves = (gridDim.x * blockDim.x) >> 4;
+  for (long long r = half; r < rows; r += halves) {
+    const uint4 qv = reinterpret_cast<const uint4*>(q + r * kD)[sub];
+    const uint4 kv = reinterpret_cast<const uint4*>(k + r * kD)[sub];
+    float sq = 0.f, sk = 0.f;
+    const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qv);
+    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = __bfloat1622float2(q2[i]);
+      const float2 c = __bfloat1622float2(k2[i]);
+      sq = fmaf(a.x, a.x, fmaf(a.y, a.y, sq));
+      sk = fmaf(c.x, c.x, fmaf(c.y, c.y, sk));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      sq += __shfl_xor_sync(hmask, sq, o);
+      sk += __shfl_xor_sync(hmask, sk, o);
+    }
+    if (sub == 0) {
+      const int hh = static_cast<int>(r % h);
+      const long long tok = r / h;
+      const int bb = static_cast<int>(tok / s);
+      const int ss = static_cast<int>(tok % s);
+      qn2[(static_cast<size_t>(bb) * h + hh) * s + ss] = sq;
+      atomicMax(&smax[bb * h + hh], __float_as_uint(sk));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < bhn; i += blockDim.x)
+    if (smax[i]) atomicMax(&kmax2_bits[i], smax[i]);
+}
+
+}  // namespace cm
+}  // namespace vomni
+
+using namespace vomni;
+
+extern "C" size_t vomni_cm_workspace_bytes(int b, int s, int h, int d) {
+  (void)d;
+  if (b <= 0 || s <= 0 || h <= 0) return 0;
+  const size_t qn = static_cast<size_t>(b) * h * s * sizeof(float);
+  const size_t km = static_cast<size_t>(b) * h * sizeof(float);
+  return align_up(qn, 256) + align_up(km, 256);
+}
+
+extern "C" int vomni_cm_prologue(const void* q, const void* k, int b, int s, int h, int d, float* qn2, float* kmax2,
+                                 vomni_stream_t stream) {
+  if (!q || !k || !qn2 || !kmax2) return VOMNI_EINVAL;
+  if (d != cm::kD || b <= 0 || s <= 0 || h <= 0) return VOMNI_EBADSHAPE;
+  if (b * h > 8192) return VOMNI_EBADSHAPE;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15) return VOMNI_EALIGN;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  VOMNI_CUDA_TRY(cudaMemsetAsync(kmax2, 0, sizeof(float) * b * h, st));
+  const long long rows = static_cast<long long>(b) * s * h;
+  const int threads = 256;
+  long long blocks = (rows * 16 + threads - 1) / threads;
+  const int max_blocks = num_sms() * 8;
+  if (blocks > max_blocks) blocks = max_blocks;
+  cm::cm_norms_kernel<<<static_cast<int>(blocks), threads, sizeof(unsigned) * b * h, st>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), b, s, h, qn2,
+      reinterpret_cast<unsigned int*>(kmax2));
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+extern "C" int vomni_cm_attend(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start,
+                               int n_keys, int h, int d, float softmax_scale, const float* qn2, const float* kmax2,
+                               float* acc_o, float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream) {
+  if (!q || !k || !v || !qn2 || !kmax2) return VOMNI_EINVAL;
+  if (d != cm::kD || b <= 0 || s_q <= 0 || h <= 0 || n_keys <= 0 || k_start < 0 || k_start + n_keys > s_kv)
+    return VOMNI_EBADSHAPE;
+  if (flags & ~(VOMNI_CM_ACC_IN | VOMNI_CM_FINAL | VOMNI_CM_OUT_DMAJOR | VOMNI_CM_LSE)) return VOMNI_EINVAL;
+  const bool final_pass = flags & VOMNI_CM_FINAL;
+  if (final_pass && !out) return VOMNI_EINVAL;
+  if ((flags & VOMNI_CM_LSE) && !lse) return VOMNI_EINVAL;
+  if ((!final_pass || (flags & VOMNI_CM_ACC_IN)) && (!acc_o || !acc_l)) return VOMNI_EINVAL;
+  if (b * h > 65535) return VOMNI_EBADSHAPE;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+                       reinterpret_cast<uintptr_t>(acc_o) | reinterpret_cast<uintptr_t>(out);
+  if (al & 15) return VOMNI_EALIGN;
+  int rc = require_sm100();
+  if (rc) return rc;
+
+  const uint64_t row_elems = static_cast<uint64_t>(h) * cm::kD;
+  CUtensorMap tq, tk, tv;
+  rc = make_tmap_3d_bf16(&tq, q, row_elems, s_q, b, 64, 128);
+  if (rc) return rc;
+  rc = make_tmap_3d_bf16(&tk, k, row_elems, s_kv, b, 64, 128);
+  if (rc) return rc;
+  rc = make_tmap_3d_bf16(&tv, v, row_elems, s_kv, b, 64, 128);
+  if (rc) return rc;
+
+  cm::Params p;
+  p.s_q = s_q;
+  p.heads = h;
+  p.n_keys = n_keys;
+  p.k_start = k_start;
+  p.scale = softmax_scale;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.qn2 = qn2;
+  p.kmax2 = kmax2;
+  p.acc_o = acc_o;
+  p.acc_l = acc_l;
+  p.out = out;
+  p.lse = lse;
+  p.flags = flags;
+  p.status = device_status_ptr();
+
+  static bool attr_set = false;
+  if (!attr_set) {
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(cm::cm_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kSmemBytes));
+    attr_set = true;
+  }
+  dim3 grid((s_q + cm::kTile - 1) / cm::kTile, b * h);
+  cm::cm_attend_kernel<<<grid, cm::kThreads, cm::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+extern "C" int vomni_cm_attention_local(const void* q, const void* k, const void* v, void* out, float* lse, int b, int s,
+                                        int h, int d, float softmax_scale, int flags, void* workspace,
+                                        size_t workspace_bytes, vomni_stream_t stream) {
+  if (!workspace) return VOMNI_EINVAL;
+  if (flags & ~(VOMNI_CM_OUT_DMAJOR | VOMNI_CM_LSE)) return VOMNI_EINVAL;
+  const size_t need = vomni_cm_workspace_bytes(b, s, h, d);
+  if (need == 0) return VOMNI_EBADSHAPE;
+  if (workspace_bytes < need) return VOMNI_EWORKSPACE;
+  float* qn2 = static_cast<float*>(workspace);
+  float* kmax2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                          align_up(static_cast<size_t>(b) * h * s * sizeof(float), 256));
+  int rc = vomni_cm_prologue(q, k, b, s, h, d, qn2, kmax2, stream);
+  if (rc) return rc;
+  return vomni_cm_attend(q, k, v, b, s, s, 0, s, h, d, softmax_scale, qn2, kmax2, nullptr, nullptr,
+                         flags | VOMNI_CM_FINAL, out, lse, stream);
+}

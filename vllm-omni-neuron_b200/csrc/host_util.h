@@ -1,0 +1,43 @@
+// Host-side helpers shared by the C-ABI translation units: error mapping, device checks,
+// TMA descriptor encoding (driver entry point fetched at run time, so the library does not link
+// libcuda directly) and the per-device status word.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/vomni_b200.h"
+
+#define VOMNI_CUDA_TRY(expr)                      \
+  do {                                            \
+    cudaError_t vomni_err_ = (expr);              \
+    if (vomni_err_ != cudaSuccess) {              \
+      vomni::set_last_cuda_error(vomni_err_);     \
+      return VOMNI_ECUDA;                         \
+    }                                             \
+  } while (0)
+
+namespace vomni {
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+void set_last_cuda_error(cudaError_t e);
+int num_sms();
+// VOMNI_OK on an sm_100 device, VOMNI_ENOTSUP otherwise.
+int require_sm100();
+// Device address of the library status word on the current device (nullptr if unavailable).
+int* device_status_ptr();
+
+// Rank-3 bf16 tensor map over a [dim2][dim1][dim0] row-major tensor, box {box0, box1, 1},
+// 128-byte swizzle, out-of-bounds elements read as zero.
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
+                      uint32_t box1);
+// Rank-2 tensor map over a [dim1][dim0] row-major tensor of 1- or 2-byte elements with an
+// explicit row pitch in bytes, box {box0, box1}, 128-byte swizzle, OOB reads as zero.
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                 uint64_t pitch_bytes, uint32_t box0, uint32_t box1);
+
+}  // namespace vomni
