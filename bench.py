@@ -1,0 +1,410 @@
+#!/usr/bin/env python
+"""Benchmark of the const-max ring attention layer (Wan2.2-A14B 480x832x81 self-attention).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2|c1|c4]
+
+One step = one self-attention layer through the public API ``wan_cp_self_attention`` (prologue
+norms + const-max attention with the d-major epilogue) over this rank's S/N query rows, with K/V
+rotated over the ring when N > 1. Default workload C2: S = 32760 tokens (latent 21x60x104, patch
+1x2x2), 40 heads x 128, bf16; Q/K/V are a seeded random-init 5120 -> 3x5120 projection of N(0,1)
+hidden states with RMSNorm on Q and K plus Wan 3-D RoPE (synthetic stand-in for the reference's
+VBench prompts). Metric: whole-job attention TFLOP/s (4*H*S^2*D per layer) and ms/layer.
+
+Under torchrun (N > 1) every rank runs one GPU of the ring (CP = N); times are device times
+(CUDA events), max over ranks. ``--impl reference`` times the reference's own CPU attention path
+(``_torch_attend``, restated in oracle/) on the host cores; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PKG = "vllm-omni-neuron_b200"
+HEADS, HEAD_DIM, HIDDEN = 40, 128, 5120
+CONFIGS = {
+    "c1": dict(S=4096, latent=None, desc="C1: single-rank full self-attention, B=1 H=40 D=128 S=4096, Q/K/V~N(0,1)*0.5"),
+    "c2": dict(S=32760, latent=(21, 60, 104), desc="C2: Wan2.2-A14B 480x832x81 self-attention, S=32760 (21x30x52 tokens), H=40 D=128"),
+    "c4": dict(S=75600, latent=(21, 90, 160), desc="C4: Wan2.2-A14B 720x1280x81 self-attention, S=75600 (21x45x80 tokens), H=40 D=128"),
+}
+METRIC = "ring-attn TFLOP/s at S=32760 (one Wan2.2-A14B self-attention layer), CP=N"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------------------ workloads
+def make_qkv(cfg: str, device, seed: int = 0):
+    """Full-sequence token-major q, k, v [1, S, 40, 128] bf16 on `device` for a config."""
+    import torch
+
+    c = CONFIGS[cfg]
+    S = c["S"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    if c["latent"] is None:
+        mk = lambda: (torch.randn(1, S, HEADS, HEAD_DIM, generator=g, device=device) * 0.5).to(torch.bfloat16)
+        return mk(), mk(), mk()
+    rope = importlib.import_module(PKG + ".rope")
+    hidden = torch.randn(1, S, HIDDEN, generator=g, device=device).to(torch.bfloat16)
+    w = (torch.randn(HIDDEN, 3 * HIDDEN, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    qkv = torch.matmul(hidden, w)  # bias 0 (wan2_2_transformer.py:1104)
+    del hidden, w
+    q, k, v = qkv.split(HIDDEN, dim=-1)
+
+    def rms(x):  # DistributedRMSNorm at TP=1, gamma=1, eps=1e-6 (wan2_2_transformer.py:879-893)
+        xf = x.float()
+        return (xf / torch.sqrt((xf * xf).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+
+    cos, sin = rope.wan_rotary_freqs(HEAD_DIM, (1, 2, 2), 1024, c["latent"], device=device)
+    q = rope.apply_rotary_emb_wan(rms(q).unflatten(2, (HEADS, HEAD_DIM)), cos, sin).contiguous()
+    k = rope.apply_rotary_emb_wan(rms(k).unflatten(2, (HEADS, HEAD_DIM)), cos, sin).contiguous()
+    v = v.unflatten(2, (HEADS, HEAD_DIM)).contiguous()
+    del qkv
+    assert q.shape[1] == S
+    return q, k, v
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples of one GPU while the timed region runs."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": mx,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ------------------------------------------------------------------------------ CPU legs
+def cpu_attention_sample(q_rows, k_full, v_full, min_seconds: float):
+    """Time the reference's CPU attention path (``_torch_attend``, wan2_2_transformer.py:640-650,
+    restated in oracle/attention.py) on a bounded sample. Returns (TFLOP/s, seconds, flops)."""
+    from oracle import attention as oat
+
+    scale = 1.0 / math.sqrt(HEAD_DIM)
+    flops_one = oat.attention_flops(1, q_rows.shape[1], q_rows.shape[2], k_full.shape[2], HEAD_DIM)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oat.torch_attend(q_rows, k_full, v_full, scale)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return flops_one * n / el / 1e12, el, flops_one * n
+
+
+def cpu_sample_arrays(q, k, v, heads: int, rows: int):
+    """[1, heads, rows, D] query sample and [1, heads, S, D] keys/values from device tensors."""
+    import numpy as np
+
+    qs = q[:, :rows, :heads].float().cpu().numpy()
+    ks = k[:, :, :heads].float().cpu().numpy()
+    vs = v[:, :, :heads].float().cpu().numpy()
+    tr = lambda x: np.ascontiguousarray(np.transpose(x, (0, 2, 1, 3)))
+    return tr(qs), tr(ks), tr(vs)
+
+
+def cpu_cores() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = max((i.get("num_threads", 0) for i in threadpool_info()), default=0)
+        if n:
+            return int(n)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=list(CONFIGS), default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = CONFIGS[args.config]
+    S = cfg["S"]
+    flops_layer = 4.0 * HEADS * S * S * HEAD_DIM
+
+    if args.impl == "reference":
+        return run_reference(args, world, rank, cfg, flops_layer)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        group = dist.group.WORLD
+    if S % world:
+        raise SystemExit(f"S={S} not divisible by {world}")
+    s_loc = S // world
+
+    pkg = importlib.import_module(PKG)
+    pkg.build()
+    lib = importlib.import_module(PKG + "._lib")
+
+    q, k, v = make_qkv(args.config, dev, seed=0)
+    sl = slice(rank * s_loc, (rank + 1) * s_loc)
+    ql, kl, vl = (x[:, sl].contiguous() for x in (q, k, v))
+    if rank != 0 or world > 1 or args.no_cpu_baseline:
+        del q, k, v
+        q = k = v = None
+    torch.cuda.synchronize()
+    scale = 1.0 / math.sqrt(HEAD_DIM)
+
+    def step(qq, kk, vv):
+        return pkg.wan_cp_self_attention(qq, kk, vv, scale, world, group, None)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- device-resident throughput
+    for _ in range(args.warmup):
+        out = step(ql, kl, vl)
+    torch.cuda.synchronize()
+    assert lib.device_status() == 0, "device status error during warm-up"
+    sampler = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = step(ql, kl, vl)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    value = flops_layer / (ms / 1e3) / 1e12
+
+    # ---------------- dominant kernel alone (events on the launching stream)
+    L = lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    qn2 = torch.empty(HEADS, s_loc, dtype=torch.float32, device=dev)
+    km = torch.empty(HEADS, dtype=torch.float32, device=dev)
+    o_tmp = torch.empty(1, HEADS, HEAD_DIM, s_loc, dtype=torch.bfloat16, device=dev)
+    lib.check(L.vomni_cm_prologue(ql.data_ptr(), kl.data_ptr(), 1, s_loc, HEADS, HEAD_DIM, qn2.data_ptr(), km.data_ptr(), st), "prologue")
+    kern_steps = max(3, min(args.steps, 10))
+    if world == 1:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(kern_steps)]
+        for a, b in evs:
+            a.record()
+            lib.check(L.vomni_cm_attend(ql.data_ptr(), kl.data_ptr(), vl.data_ptr(), 1, s_loc, s_loc, 0, s_loc, HEADS, HEAD_DIM, scale,
+                                        qn2.data_ptr(), km.data_ptr(), None, None, lib.CM_FINAL | lib.CM_OUT_DMAJOR, o_tmp.data_ptr(), None, st), "attend")
+            b.record()
+        torch.cuda.synchronize()
+        kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        kern_flops = 4.0 * HEADS * s_loc * s_loc * HEAD_DIM
+    else:
+        kern_ms, kern_flops = None, None
+    peaks = {}
+    pk_path = ROOT / "MEASURED_PEAKS.json"
+    if pk_path.exists():
+        peaks = json.loads(pk_path.read_text())
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    peak_src = "measured (bf16_tflops_sustained)" if peaks.get("bf16_tflops_sustained") else "fallback"
+    traffic = None
+    tr_path = ROOT / "profiles" / "cm_attend_traffic.json"
+    if tr_path.exists() and kern_flops:
+        t = json.loads(tr_path.read_text())
+        # dram bytes per (query-tile x key-tile) pair, scaled to this launch's tile pairs
+        pairs = math.ceil(s_loc / 128) * math.ceil(s_loc / 128) * HEADS
+        traffic = t["dram_bytes_per_tile_pair"] * pairs
+    roof = None
+    if kern_ms:
+        ach = kern_flops / (kern_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s", "frac": round(ach / peak, 4),
+                "traffic": traffic, "kernel": "cm_attend_kernel", "kernel_ms": round(kern_ms, 4), "peak_source": peak_src}
+
+    # ---------------- end to end through the public API with host buffers
+    qh, kh, vh = (x.cpu().pin_memory() for x in (ql, kl, vl))
+    out_h = torch.empty((1, HEADS, HEAD_DIM, s_loc), dtype=torch.bfloat16).pin_memory()
+    qd, kd, vd = (torch.empty_like(x) for x in (ql, kl, vl))
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        o = step(qd, kd, vd)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1)) / e2e_steps
+    bi = 3 * s_loc * HEADS * HEAD_DIM * 2
+    bo = s_loc * HEADS * HEAD_DIM * 2
+    assert lib.device_status() == 0, "device status error"
+
+    # ---------------- CPU baseline (rank 0, N == 1)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        heads_s, rows_s = 1, 512
+        qs, ks, vs = cpu_sample_arrays(q, k, v, heads_s, rows_s)
+        val, el, fl = cpu_attention_sample(qs, ks, vs, min_seconds=10.0)
+        cpu = {"value": round(val, 5), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
+               "sample": f"_torch_attend restated (oracle/attention.py torch_attend, numpy fp32): {heads_s} head x {rows_s} query rows x {S} keys, repeated {el:.1f}s ({fl/1e9:.0f} GFLOP)"}
+
+    launches_per_step = 2  # cm_norms_kernel + cm_attend_kernel
+    if world > 1:
+        launches_per_step = 2 + world - 1  # prologue + one attention pass per ring phase (upper bound)
+    res = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; random-init projection + RMSNorm + 3-D RoPE, no checkpoint/prompts)",
+        "config": {
+            "workload": cfg["desc"],
+            "S": S, "heads": HEADS, "head_dim": HEAD_DIM, "cp": world, "s_loc": s_loc,
+            "step": "one self-attention layer via wan_cp_self_attention (prologue + const-max attention, d-major out)",
+            "l2": f"inputs larger than L2 (Q/K/V {3 * s_loc * HEADS * HEAD_DIM * 2 / 1e6:.0f} MB per rank per step)",
+            "flops_per_layer": flops_layer,
+        },
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "e2e": {"value": round(flops_layer / (e2e_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo},
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args, world, rank, cfg, flops_layer):
+    """The reference arm: the reference's own CPU attention path on the host cores."""
+    if rank != 0:
+        return
+    import numpy as np
+
+    S = cfg["S"]
+    rng = np.random.default_rng(0)
+    heads_s, rows_s = 1, 1024
+    # Same shapes/distribution as the workload rows (unit-RMS rows after RMSNorm + RoPE).
+    mk = lambda n: (rng.standard_normal((1, heads_s, n, HEAD_DIM)).astype(np.float32))
+    qs, ks, vs = mk(rows_s), mk(S), mk(S)
+    from oracle.numerics import bf16_round
+
+    qs, ks, vs = bf16_round(qs), bf16_round(ks), bf16_round(vs)
+    for _ in range(args.warmup):
+        cpu_attention_sample(qs, ks, vs, min_seconds=0.0)
+    t0 = time.perf_counter()
+    tot_fl = 0.0
+    for _ in range(args.steps):
+        _, _, fl = cpu_attention_sample(qs, ks, vs, min_seconds=0.0)
+        tot_fl += fl
+    el = time.perf_counter() - t0
+    val = tot_fl / el / 1e12
+    sample = (f"_torch_attend (wan2_2_transformer.py:640-650) restated in oracle/attention.py, numpy fp32, "
+              f"{heads_s} head x {rows_s} query rows x {S} keys per step")
+    res = {
+        "metric": METRIC, "value": round(val, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(flops_layer / (val * 1e12) * 1e3, 3) if val else None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["desc"], "S": S, "heads": HEADS, "head_dim": HEAD_DIM, "cp": world},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(val, 6), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port", "sample": sample},
+        "e2e": {"value": round(val, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()
