@@ -93,6 +93,22 @@ VOMNI_API int vomni_cm_attention_local(const void* q, const void* k, const void*
                              int d, float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
                              vomni_stream_t stream);
 
+/* Allocation-free single-rank const-max attention. No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory — a plugin running inside a host runtime that owns the
+ * whole device heap, or a latency-critical path that must not take cudaMalloc's implicit device
+ * synchronisation. Same computation and arguments as vomni_cm_attention_local, but the prologue
+ * scratch lives in a library-owned static device array of 8 MiB (held on every device that loads
+ * the library until the process exits), so the call allocates nothing; the caller still passes
+ * q, k, v, out (and lse). Limit: vomni_cm_workspace_bytes(b, s, h, d) <= 8 MiB (about
+ * b*h*s <= 2.09 million query rows); larger shapes return VOMNI_EWORKSPACE.
+ * The first call on a device looks up the array's device address with that device current; make
+ * that first call before any stream capture. All calls share the one array and it keeps the last
+ * call's contents (the key-max slots are cleared by each call before use): calls that overlap on
+ * the GPU (different streams, or threads without ordering) race on it. */
+VOMNI_API int vomni_cm_attention_local_noalloc(const void* q, const void* k, const void* v, void* out, float* lse, int b,
+                                               int s, int h, int d, float softmax_scale, int flags,
+                                               vomni_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

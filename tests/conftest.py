@@ -24,7 +24,9 @@ def load_pkg():
 
 @pytest.fixture(scope="session")
 def pkg():
-    return load_pkg()
+    p = load_pkg()
+    p.build()  # no-op when libvomni_b200.so is newer than its sources
+    return p
 
 
 @pytest.fixture(scope="session")

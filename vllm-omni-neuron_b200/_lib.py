@@ -32,6 +32,10 @@ SIGNATURES = {
         c_int,
         [P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_int, P, c_size_t, P],
     ),
+    "vomni_cm_attention_local_noalloc": (
+        c_int,
+        [P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_int, P],
+    ),
 }
 
 # flags (include/vomni_b200.h)

@@ -23,6 +23,8 @@
 #include "common.cuh"
 #include "host_util.h"
 
+#include <mutex>
+
 namespace vomni {
 namespace cm {
 
@@ -440,4 +442,48 @@ extern "C" int vomni_cm_attention_local(const void* q, const void* k, const void
   if (rc) return rc;
   return vomni_cm_attend(q, k, v, b, s, s, 0, s, h, d, softmax_scale, qn2, kmax2, nullptr, nullptr,
                          flags | VOMNI_CM_FINAL, out, lse, stream);
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory: a plugin inside a host runtime that owns the whole
+// device heap (an inference server's pool, a C plugin ABI with no allocator hook), or a
+// latency-critical path that must not hit cudaMalloc's implicit device synchronisation. For them
+// the prologue scratch (per-token ||q||^2 and per-head max ||k||^2) lives in this file-scope array
+// instead of a caller workspace: 8 MiB on every device that loads the library, held until exit.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_cm_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+void* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device. The array's name is only a host-side
+// stand-in, so the address is looked up once per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  VOMNI_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return VOMNI_ENOTSUP;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_scratch_ptr[dev]) {
+    void* p = nullptr;
+    VOMNI_CUDA_TRY(cudaGetSymbolAddress(&p, g_cm_noalloc_scratch));
+    g_noalloc_scratch_ptr[dev] = p;
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return VOMNI_OK;
+}
+}  // namespace
+
+extern "C" int vomni_cm_attention_local_noalloc(const void* q, const void* k, const void* v, void* out, float* lse, int b,
+                                                int s, int h, int d, float softmax_scale, int flags,
+                                                vomni_stream_t stream) {
+  const size_t need = vomni_cm_workspace_bytes(b, s, h, d);
+  if (need == 0) return VOMNI_EBADSHAPE;
+  if (need > kNoAllocScratchBytes) return VOMNI_EWORKSPACE;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // The prologue clears the key-max slots before it max-accumulates; qn2 is fully overwritten.
+  return vomni_cm_attention_local(q, k, v, out, lse, b, s, h, d, softmax_scale, flags, scratch, need, stream);
 }
