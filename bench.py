@@ -285,9 +285,8 @@ def main():
     tr_path = ROOT / "profiles" / "cm_attend_traffic.json"
     if tr_path.exists() and kern_flops:
         t = json.loads(tr_path.read_text())
-        # dram bytes per (query-tile x key-tile) pair, scaled to this launch's tile pairs
-        pairs = math.ceil(s_loc / 128) * math.ceil(s_loc / 128) * HEADS
-        traffic = t["dram_bytes_per_tile_pair"] * pairs
+        # DRAM bytes per (token, head) from a small-case ncu capture, scaled to this launch
+        traffic = round(t["dram_bytes_per_token_head"] * s_loc * HEADS)
     roof = None
     if kern_ms:
         ach = kern_flops / (kern_ms / 1e3) / 1e12
