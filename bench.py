@@ -263,7 +263,7 @@ def main():
     o_tmp = torch.empty(1, HEADS, HEAD_DIM, s_loc, dtype=torch.bfloat16, device=dev)
     lib.check(L.vomni_cm_prologue(ql.data_ptr(), kl.data_ptr(), 1, s_loc, HEADS, HEAD_DIM, qn2.data_ptr(), km.data_ptr(), st), "prologue")
     kern_steps = max(3, min(args.steps, 10))
-    if world == 1:
+    if True:  # the local-block pass: at N > 1 the largest single launch of the step
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(kern_steps)]
         for a, b in evs:
             a.record()
@@ -273,8 +273,6 @@ def main():
         torch.cuda.synchronize()
         kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
         kern_flops = 4.0 * HEADS * s_loc * s_loc * HEAD_DIM
-    else:
-        kern_ms, kern_flops = None, None
     peaks = {}
     pk_path = ROOT / "MEASURED_PEAKS.json"
     if pk_path.exists():
@@ -333,7 +331,8 @@ def main():
 
     launches_per_step = 2  # cm_norms_kernel + cm_attend_kernel
     if world > 1:
-        launches_per_step = 2 + world - 1  # prologue + one attention pass per ring phase (upper bound)
+        ring = importlib.import_module(PKG + ".ring")
+        launches_per_step = 1 + len(ring.phase_plan(world))  # prologue + one attention pass per ring pass
     res = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -364,6 +363,7 @@ def main():
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
+        pkg.destroy_rings()
         dist.destroy_process_group()
 
 

@@ -93,6 +93,39 @@ VOMNI_API int vomni_cm_attention_local(const void* q, const void* k, const void*
                              int d, float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
                              vomni_stream_t stream);
 
+/* ------------------------------------------------------------------ context-parallel ring
+ * Replaces the ring driver of ring_attention_const_max_fwd(num_workers = N > 1)
+ * (ring_attention_const_max_fwd.py:1196-1205 all_reduce(max) of the key norm, :1287-1398 K/V
+ * rotation and per-step accumulation) and its replica-group registration
+ * (diffusion/distributed/parallel_state.py:180-188, 355-415).
+ *
+ * One vomni_ring per CP group per process (one process per GPU). Creation is collective over the
+ * group: every rank calls it with the same NCCL unique id (rank 0 makes it with
+ * vomni_nccl_unique_id and the host broadcasts the bytes) and the same (b, s_max, h, d); it creates
+ * an NCCL communicator, allocates the registered send buffer (exported to the peers by CUDA IPC),
+ * the gather buffer and the workspace. Every call of vomni_ring_attention is collective too, in the
+ * same order on every rank. */
+typedef struct vomni_ring vomni_ring;
+
+VOMNI_API int vomni_nccl_unique_id(void* out, size_t bytes);
+VOMNI_API int vomni_ring_create(vomni_ring** out, int rank, int world, const void* nccl_id, size_t id_bytes, int b,
+                                int s_max, int h, int d);
+VOMNI_API int vomni_ring_destroy(vomni_ring* ring);
+/* VOMNI_OK, or VOMNI_ENCCL / VOMNI_ESTATE once the communicator reported an asynchronous error. */
+VOMNI_API int vomni_ring_check(vomni_ring* ring);
+/* q, k, v: this rank's token-major [b, s_loc, h, d] shard (s_loc <= s_max). out: head-major
+ * [b, h, s_loc, d] or d-major with VOMNI_CM_OUT_DMAJOR; lse with VOMNI_CM_LSE. */
+VOMNI_API int vomni_ring_attention(vomni_ring* ring, const void* q, const void* k, const void* v, void* out, float* lse,
+                                   int b, int s_loc, int h, int d, float softmax_scale, int flags,
+                                   vomni_stream_t stream);
+/* Pass plan (host-only, no GPU): pass 0 is the local block; pass i >= 1 covers gather slots
+ * [first[i], first[i] + count[i]) with counts 1, 2, 4, ...; slot j holds ring step j + 1.
+ * Returns the number of passes, or a negative status. */
+VOMNI_API int vomni_ring_phase_plan(int world, int* first, int* count, int max_phases);
+/* Rank whose block ring step `step` consumes on `rank`: (rank - step) mod world (the reference's
+ * collective_permute forwards each block to the next rank, ring_attention_const_max_fwd.py:130-144). */
+VOMNI_API int vomni_ring_source_rank(int rank, int world, int step);
+
 /* Allocation-free single-rank const-max attention. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory — a plugin running inside a host runtime that owns the
  * whole device heap, or a latency-critical path that must not take cudaMalloc's implicit device

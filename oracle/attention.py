@@ -70,6 +70,49 @@ def const_max_bounds(qs, ks, scale: float):
     return qn2, kmax2, cs
 
 
+def const_max_partial(q_tok, k_tok, v_tok, c, scale: float, scores_bf16: bool = False, q_block: int = 512):
+    """One ring step / pass (attention_const_max.py:138-234): unnormalised ``[sum P V | sum P]`` of the
+    query rows ``q_tok [b, Sq, h, d]`` against ``k_tok / v_tok [b, Sk, h, d]`` with the per-row bound
+    ``c [b, h, Sq]``. Returns (acc [b, h, Sq, d] fp32, sums [b, h, Sq] fp32)."""
+    qh = np.transpose(q_tok, (0, 2, 1, 3)).astype(np.float32)
+    kh = np.transpose(k_tok, (0, 2, 1, 3)).astype(np.float32)
+    vh = np.transpose(v_tok, (0, 2, 1, 3)).astype(np.float32)
+    b, h, sq, d = qh.shape
+    q_s = bf16_round(qh * np.float32(scale))
+    acc = np.zeros((b, h, sq, vh.shape[-1]), np.float32)
+    ssum = np.zeros((b, h, sq), np.float32)
+    for bi in range(b):
+        for hi in range(h):
+            kt = kh[bi, hi].T
+            for s0 in range(0, sq, q_block):
+                sl = slice(s0, s0 + q_block)
+                sc = q_s[bi, hi, sl] @ kt
+                if scores_bf16:
+                    sc = bf16_round(sc)
+                shifted = fp16_round(sc - c[bi, hi, sl][:, None])
+                p = bf16_round(np.exp(shifted))
+                acc[bi, hi, sl] += p @ vh[bi, hi]
+                ssum[bi, hi, sl] += p.sum(axis=-1)
+    return acc, ssum
+
+
+def const_max_normalize(acc, ssum, c=None, training: bool = False):
+    """o = bf16(acc / max(sum, 1e-37)) and lse = c + log(max(sum, 1e-37)) in the [b, h, 128, groups]
+    layout (ring_attention_const_max_fwd.py:655-804)."""
+    clamped = np.maximum(ssum, np.float32(SUM_CLAMP))
+    o = bf16_round(acc * (np.float32(1.0) / clamped)[..., None])
+    if not training:
+        return o
+    b, h, s_loc = ssum.shape
+    groups = -(-s_loc // 128)
+    lse_tok = c + np.log(clamped)
+    lse = np.zeros((b, h, 128, groups), np.float32)
+    for g in range(groups):
+        rows = min(128, s_loc - g * 128)
+        lse[:, :, :rows, g] = lse_tok[:, :, g * 128:g * 128 + rows]
+    return o, lse
+
+
 def const_max_ring_attention(
     qs,
     ks,
@@ -91,37 +134,19 @@ def const_max_ring_attention(
     _, _, cs = const_max_bounds(qs, ks, scale)
     outs, lses = [], []
     for r in range(n):
-        qh = np.transpose(qs[r], (0, 2, 1, 3)).astype(np.float32)  # [b,h,S,d]
-        q_s = bf16_round(qh * np.float32(scale))
         acc = np.zeros((b, h, s_loc, d), np.float32)
         ssum = np.zeros((b, h, s_loc), np.float32)
         for step in range(n):
             src = (r - step) % n
-            kh = np.transpose(ks[src], (0, 2, 1, 3)).astype(np.float32)
-            vh = np.transpose(vs[src], (0, 2, 1, 3)).astype(np.float32)
-            for bi in range(b):
-                for hi in range(h):
-                    kt = kh[bi, hi].T
-                    for s0 in range(0, s_loc, q_block):
-                        sl = slice(s0, s0 + q_block)
-                        sc = q_s[bi, hi, sl] @ kt
-                        if scores_bf16:
-                            sc = bf16_round(sc)
-                        shifted = fp16_round(sc - cs[r][bi, hi, sl][:, None])
-                        p = bf16_round(np.exp(shifted))
-                        acc[bi, hi, sl] += p @ vh[bi, hi]
-                        ssum[bi, hi, sl] += p.sum(axis=-1)
-        clamped = np.maximum(ssum, np.float32(SUM_CLAMP))
-        o = bf16_round(acc * (np.float32(1.0) / clamped)[..., None])
-        outs.append(o)
+            a, sm = const_max_partial(qs[r], ks[src], vs[src], cs[r], scale, scores_bf16, q_block)
+            acc += a
+            ssum += sm
+        res = const_max_normalize(acc, ssum, cs[r], training)
         if training:
-            groups = -(-s_loc // 128)
-            lse_tok = cs[r] + np.log(clamped)
-            lse = np.zeros((b, h, 128, groups), np.float32)
-            for g in range(groups):
-                rows = min(128, s_loc - g * 128)
-                lse[:, :, :rows, g] = lse_tok[:, :, g * 128:g * 128 + rows]
-            lses.append(lse)
+            outs.append(res[0])
+            lses.append(res[1])
+        else:
+            outs.append(res)
     if training:
         return outs, lses
     return outs

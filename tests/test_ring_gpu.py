@@ -1,0 +1,94 @@
+"""Multi-GPU ring attention (one process per GPU, NCCL) against the CPU oracle.
+Skips unless at least two CUDA devices are visible."""
+
+import math
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _shard(rank, b, s, h, seed=21):
+    g = torch.Generator().manual_seed(seed + rank)
+    return [(torch.randn(b, s, h, 128, generator=g) * 0.6).to(torch.bfloat16) for _ in range(3)]
+
+
+def _worker(rank, world, port, shapes, out_q):
+    try:
+        from datetime import timedelta
+        from importlib import import_module
+
+        import torch.distributed as dist
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        pkg = import_module("vllm-omni-neuron_b200")
+        lib = import_module("vllm-omni-neuron_b200._lib")
+        from oracle import attention as oat
+
+        errs = []
+        for (b, s, h) in shapes:
+            shards = [_shard(r, b, s, h) for r in range(world)]
+            q, k, v = (x.to(dev) for x in shards[rank])
+            for call in range(2):  # two calls: exercises both send-buffer parities
+                o, lse = pkg.ring_attention_const_max_fwd(q, k, v, num_workers=world, training=True)
+                od = pkg.wan_cp_self_attention(q, k, v, 1 / math.sqrt(128), world, dist.group.WORLD, None)
+            torch.cuda.synchronize()
+            f = lambda t: t.float().cpu().numpy()
+            qs, ks, vs = ([f(sh[i]) for sh in shards] for i in range(3))
+            ref_o, ref_l = oat.const_max_ring_attention(qs, ks, vs, training=True)
+            exact = oat.wan_cp_self_attention_oracle(qs, ks, vs, 1 / math.sqrt(128))[rank]
+            got = f(o).astype(np.float64)
+            r = ref_o[rank].astype(np.float64)
+            cos = (got * r).sum() / math.sqrt((got * got).sum() * (r * r).sum())
+            errs.append(("cos_ring", (b, s, h), float(cos)))
+            errs.append(("max_ring", (b, s, h), float(np.abs(got - r).max())))
+            errs.append(("max_exact_dmajor", (b, s, h), float(np.abs(f(od) - exact).max())))
+            errs.append(("max_lse", (b, s, h), float(np.abs(f(lse) - ref_l[rank]).max())))
+        status = lib.device_status()
+        pkg.destroy_rings()
+        dist.destroy_process_group()
+        out_q.put((rank, errs, status, None))
+    except Exception:
+        out_q.put((rank, None, None, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+def test_ring_multi_gpu():
+    world = min(torch.cuda.device_count(), 4)
+    shapes = [(1, 256, 2), (1, 200, 3), (2, 130, 1)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shapes, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, errs, status, tb in res:
+        assert tb is None, tb
+        assert status == 0
+        for name, shape, val in errs:
+            if name.startswith("cos"):
+                assert val >= 0.9999, (rank, name, shape, val)
+            elif name == "max_lse":
+                assert val <= 3e-2, (rank, name, shape, val)
+            else:
+                assert val <= 2e-2, (rank, name, shape, val)

@@ -13,10 +13,12 @@ Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``
 
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .build import build
+from .ring import destroy_rings
 
 __all__ = [
     "attention_local",
     "build",
+    "destroy_rings",
     "ring_attention_const_max_fwd",
     "wan_cp_self_attention",
 ]

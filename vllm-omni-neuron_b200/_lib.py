@@ -32,6 +32,16 @@ SIGNATURES = {
         c_int,
         [P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_int, P, c_size_t, P],
     ),
+    "vomni_nccl_unique_id": (c_int, [P, c_size_t]),
+    "vomni_ring_create": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, P, c_size_t, c_int, c_int, c_int, c_int]),
+    "vomni_ring_destroy": (c_int, [P]),
+    "vomni_ring_check": (c_int, [P]),
+    "vomni_ring_attention": (
+        c_int,
+        [P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_int, P],
+    ),
+    "vomni_ring_phase_plan": (c_int, [c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_int]),
+    "vomni_ring_source_rank": (c_int, [c_int, c_int, c_int]),
     "vomni_cm_attention_local_noalloc": (
         c_int,
         [P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_int, P],
