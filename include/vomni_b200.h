@@ -93,6 +93,22 @@ VOMNI_API int vomni_cm_attention_local(const void* q, const void* k, const void*
                              int d, float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
                              vomni_stream_t stream);
 
+/* ------------------------------------------------------------------ fused adaLN + FP8 quant
+ * Replaces adaln_quant_kernel (kernels/nkilib/experimental/norm/adaln_quant.py:117-810) as called
+ * by the bridge adaln_modulate (diffusion/quantization/adaln_kernels.py:87-201):
+ *   t = residual + gate * hidden (fp32, rounded to bf16 -> residual_out); xhat = LayerNorm(t) |
+ *   RMSNorm(t) | t; y = xhat * mul + add; out = bf16(y) | FP8 row quant | FP8 MX-32.
+ * hidden/residual/residual_out: bf16 [rows, h]; mul/add: bf16 [n_mod, h]; gate: fp32 [n_mod, h]
+ * (n_mod = rows / rows_per_mod; all optional except hidden). norm_type 0 layer / 1 rms / 2 none.
+ * quant 0: out bf16 [rows, h]. quant 1 (row, range 448 if ocp else 240): packed != 0 -> out u8
+ * [rows, h + 4] (codes, then the fp32 dequant scale, adaln_quant.py:540-565); packed == 0 -> out u8
+ * [rows, h] + out_scale fp32 [rows]. quant 2 (MX-32, adaln_quant_torch.py:151-175): out u8
+ * [rows, h] e4m3fn codes + out_scale u8 [rows, h/32] UE8M0 exponents. h <= 16384, h % 8 == 0. */
+VOMNI_API int vomni_adaln_modulate(const void* hidden, const void* residual, const void* mul, const void* add,
+                                   const float* gate, long long rows, int h, long long rows_per_mod, float eps,
+                                   int norm_type, int quant, int ocp, int packed, void* out, void* out_scale,
+                                   void* residual_out, vomni_stream_t stream);
+
 /* ------------------------------------------------------------------ context-parallel ring
  * Replaces the ring driver of ring_attention_const_max_fwd(num_workers = N > 1)
  * (ring_attention_const_max_fwd.py:1196-1205 all_reduce(max) of the key norm, :1287-1398 K/V

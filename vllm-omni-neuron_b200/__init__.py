@@ -11,11 +11,13 @@ Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``
 :func:`build`.
 """
 
+from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .build import build
 from .ring import destroy_rings
 
 __all__ = [
+    "adaln_modulate",
     "attention_local",
     "build",
     "destroy_rings",

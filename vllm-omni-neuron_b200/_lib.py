@@ -32,6 +32,10 @@ SIGNATURES = {
         c_int,
         [P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_int, P, c_size_t, P],
     ),
+    "vomni_adaln_modulate": (
+        c_int,
+        [P, P, P, P, P, ctypes.c_longlong, c_int, ctypes.c_longlong, c_float, c_int, c_int, c_int, c_int, P, P, P, P],
+    ),
     "vomni_nccl_unique_id": (c_int, [P, c_size_t]),
     "vomni_ring_create": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, P, c_size_t, c_int, c_int, c_int, c_int]),
     "vomni_ring_destroy": (c_int, [P]),
