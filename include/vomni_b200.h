@@ -109,6 +109,29 @@ VOMNI_API int vomni_adaln_modulate(const void* hidden, const void* residual, con
                                    int norm_type, int quant, int ocp, int packed, void* out, void* out_scale,
                                    void* residual_out, vomni_stream_t stream);
 
+/* ------------------------------------------------------------------ FP8 QKV projection
+ * Replaces qkv(quantization_type=ROW_MX) -> _qkv_cte_mx_impl (kernels/nkilib/core/qkv/qkv_cte.py:
+ * 2725-3993) as called through torch_compatible_row_mx_qkv (kernels/qkv_shim.py:26-77) by
+ * row_mx_qkv_proj (diffusion/quantization/row_mx_kernels.py:48-111).
+ *
+ * vomni_qkv_fp8_gemm: y[t, i] = bf16(sum_h x[t, h] w[i, h] * row_scale[t] * chan_scale[i] + bias[i])
+ * (_dequant_row_mx, qkv_cte.py:3996-4021). x_codes: e4m3fn [t, h]; w_codes: e4m3fn [i, h] (K-major);
+ * bias bf16 [i] or NULL; y bf16 [t, i]. If sumsq is non-NULL it receives, per row, the partial sums
+ * of squares of the stored bf16 y over each 256-column tile of the Q and K segments
+ * ([t, (q_dim + kv_dim) / 256] fp32), the input of the across-heads RMS (qkv_cte.py:3870-3898).
+ * h % 128 == 0, i % 256 == 0, q_dim % 256 == 0, kv_dim % 256 == 0. */
+VOMNI_API int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, const void* w_codes,
+                                 const float* chan_scale, const void* bias, int t, int h, int i, int q_dim, int kv_dim,
+                                 void* y, float* sumsq, vomni_stream_t stream);
+/* In place on y [t, i]: inv = rsqrt(sum(sumsq row segment) / (heads * 128) + eps) for the Q and K
+ * segments; x * gamma (bf16 [heads*128], optional); then rotate-half RoPE with inv folded in
+ * (cos/sin fp32 [t, 128], optional: without them x * inv) — the apply pass of qkv_cte.py:3903-3991. */
+VOMNI_API int vomni_qk_norm_rope(void* y, int t, int i, int q_heads, int kv_heads, int head_dim, const float* sumsq,
+                                 float eps, const void* gamma_q, const void* gamma_k, const float* cos, const float* sin,
+                                 vomni_stream_t stream);
+/* [t, h + 4] packed rows (adaln ROW output) -> codes [t, h] + scales [t]. */
+VOMNI_API int vomni_qkv_unpack_rows(const void* packed, int t, int h, void* codes, float* scales, vomni_stream_t stream);
+
 /* ------------------------------------------------------------------ context-parallel ring
  * Replaces the ring driver of ring_attention_const_max_fwd(num_workers = N > 1)
  * (ring_attention_const_max_fwd.py:1196-1205 all_reduce(max) of the key norm, :1287-1398 K/V

@@ -14,6 +14,7 @@ Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``
 from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .build import build
+from .qkv import quantize_qkv_weight, repack_mx_contiguous, row_mx_qkv_proj
 from .ring import destroy_rings
 
 __all__ = [
@@ -21,6 +22,9 @@ __all__ = [
     "attention_local",
     "build",
     "destroy_rings",
+    "quantize_qkv_weight",
+    "repack_mx_contiguous",
     "ring_attention_const_max_fwd",
+    "row_mx_qkv_proj",
     "wan_cp_self_attention",
 ]

@@ -36,6 +36,9 @@ SIGNATURES = {
         c_int,
         [P, P, P, P, P, ctypes.c_longlong, c_int, ctypes.c_longlong, c_float, c_int, c_int, c_int, c_int, P, P, P, P],
     ),
+    "vomni_qkv_fp8_gemm": (c_int, [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P]),
+    "vomni_qk_norm_rope": (c_int, [P, c_int, c_int, c_int, c_int, c_int, P, c_float, P, P, P, P, P]),
+    "vomni_qkv_unpack_rows": (c_int, [P, c_int, c_int, P, P, P]),
     "vomni_nccl_unique_id": (c_int, [P, c_size_t]),
     "vomni_ring_create": (c_int, [ctypes.POINTER(c_void_p), c_int, c_int, P, c_size_t, c_int, c_int, c_int, c_int]),
     "vomni_ring_destroy": (c_int, [P]),
