@@ -36,6 +36,7 @@ HEADS, HEAD_DIM, HIDDEN = 40, 128, 5120
 CONFIGS = {
     "c1": dict(S=4096, latent=None, desc="C1: single-rank full self-attention, B=1 H=40 D=128 S=4096, Q/K/V~N(0,1)*0.5"),
     "c2": dict(S=32760, latent=(21, 60, 104), desc="C2: Wan2.2-A14B 480x832x81 self-attention, S=32760 (21x30x52 tokens), H=40 D=128"),
+    "c3": dict(S=32760, latent=None, desc="C3: fused adaLN (LayerNorm eps 1e-6, shift/scale) + FP8 row quant + FP8 QKV projection, T=32760 H=5120 I=15360"),
     "c4": dict(S=75600, latent=(21, 90, 160), desc="C4: Wan2.2-A14B 720x1280x81 self-attention, S=75600 (21x45x80 tokens), H=40 D=128"),
 }
 METRIC = "ring-attn TFLOP/s at S=32760 (one Wan2.2-A14B self-attention layer), CP=N"
@@ -177,6 +178,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=list(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0, help="C3 only: override T (small case for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -190,6 +192,8 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, world, rank, cfg, flops_layer)
+    if args.config == "c3":
+        return run_c3(args)
 
     import torch
     import torch.distributed as dist
@@ -365,6 +369,95 @@ def main():
     if world > 1:
         pkg.destroy_rings()
         dist.destroy_process_group()
+
+
+def run_c3(args):
+    """C3 block: adaLN + FP8 row quant (HBM-bound) then the FP8 QKV GEMM (tensor-bound) and the
+    across-heads norm + RoPE apply (HBM-bound). Prints one JSON line with each kernel's roofline."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module(PKG)
+    pkg.build()
+    lib = importlib.import_module(PKG + "._lib")
+    rope = importlib.import_module(PKG + ".rope")
+    T, H, I = (args.tokens or 32760), HIDDEN, 3 * HIDDEN
+    g = torch.Generator(device=dev).manual_seed(0)
+    hidden = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    mods = torch.randn(6, H, generator=g, device=dev) * 0.1
+    mul, add = (1 + mods[1]).to(torch.bfloat16), mods[0].to(torch.bfloat16)
+    w = torch.randn(H, I, generator=g, device=dev) * 0.02
+    wq, chan = pkg.quantize_qkv_weight(w, H, H)
+    bias = torch.zeros(I, dtype=torch.bfloat16, device=dev)
+    cos, sin = rope.wan_rotary_freqs(HEAD_DIM, (1, 2, 2), 1024, (21, 60, 104), device=dev)
+    cos_rh, sin_rh = (x.reshape(-1, HEAD_DIM)[:T].contiguous() for x in rope.rope_rotate_half_caches(cos, sin))
+    gamma = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    L = lib.load()
+    codes = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=dev)
+    scales = torch.empty(T, dtype=torch.float32, device=dev)
+    y = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
+    sumsq = torch.empty(T, 2 * H // 256, dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2: flushed between launches
+
+    def adaln():
+        lib.check(L.vomni_adaln_modulate(hidden.data_ptr(), None, mul.data_ptr(), add.data_ptr(), None, T, H, T, 1e-6, 0, 1, 1, 0,
+                                         codes.data_ptr(), scales.data_ptr(), None, st), "adaln")
+
+    def gemm():
+        lib.check(L.vomni_qkv_fp8_gemm(codes.data_ptr(), scales.data_ptr(), wq.data_ptr(), chan.data_ptr(), bias.data_ptr(),
+                                       T, H, I, H, H, y.data_ptr(), sumsq.data_ptr(), st), "gemm")
+
+    def apply():
+        lib.check(L.vomni_qk_norm_rope(y.data_ptr(), T, I, HEADS, HEADS, HEAD_DIM, sumsq.data_ptr(), 1e-6, gamma.data_ptr(),
+                                       gamma.data_ptr(), cos_rh.data_ptr(), sin_rh.data_ptr(), st), "apply")
+
+    def timeit(fn, n):
+        ts = []
+        for _ in range(n):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    for fn in (adaln, gemm, apply):
+        for _ in range(args.warmup):
+            fn()
+    torch.cuda.synchronize()
+    n = max(args.steps, 5)
+    sampler = ClockSampler(0)
+    sampler.start()
+    t_ad, t_gm, t_ap = timeit(adaln, n), timeit(gemm, n), timeit(apply, n)
+    clocks = sampler.stop()
+    assert lib.device_status() == 0
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    ad_bytes = 2 * T * H + T * H + 4 * T
+    ap_bytes = 2 * (2 * T * 2 * H) + T * (2 * H // 256) * 4 + 2 * T * HEAD_DIM * 4
+    gm_flops = 2.0 * T * H * I
+    res = {
+        "metric": "C3 fused adaLN + FP8 row quant + FP8 QKV projection (ms per call, per kernel)",
+        "value": round(t_ad + t_gm + t_ap, 4), "unit": "ms", "higher_is_better": False, "n_gpus": 1,
+        "steps": n, "warmup": args.warmup, "dtype": "fp8 e4m3 (ROW scales) / bf16 I/O", "data": "synthetic",
+        "config": {"workload": CONFIGS["c3"]["desc"], "T": T, "H": H, "I": I, "l2": "flushed (256 MB write) before each launch"},
+        "kernels": {
+            "adaln_rowquant": {"ms": round(t_ad, 4), "bytes": ad_bytes, "GB/s": round(ad_bytes / t_ad / 1e6, 1),
+                               "frac_of_measured_hbm": round(ad_bytes / t_ad / 1e6 / hbm, 4)},
+            "qkv_fp8_gemm": {"ms": round(t_gm, 4), "flops": gm_flops, "TFLOP/s": round(gm_flops / t_gm / 1e9, 1),
+                             "frac_of_measured_bf16_burst_x2": round(gm_flops / t_gm / 1e9 / (2 * bf16), 4)},
+            "qk_norm_rope": {"ms": round(t_ap, 4), "bytes": ap_bytes, "GB/s": round(ap_bytes / t_ap / 1e6, 1),
+                             "frac_of_measured_hbm": round(ap_bytes / t_ap / 1e6 / hbm, 4)},
+        },
+        "clocks": clocks,
+        "gpu_launches": 3 * n,
+    }
+    print(json.dumps(res), flush=True)
 
 
 def run_reference(args, world, rank, cfg, flops_layer):

@@ -36,9 +36,10 @@ def _normalize(x: np.ndarray, norm_type: str, eps: float) -> np.ndarray:
     raise ValueError(f"unsupported norm_type {norm_type!r}")
 
 
-def row_quantize(y: np.ndarray, ocp: bool = True, lower_bound: float = 0.0):
+def row_quantize(y: np.ndarray, ocp: bool = True, lower_bound: float = 0.0, reciprocal: bool = False):
     """Per-row FP8 quant, adaln_quant_torch.py:133-145: scale = max(amax/range, 1e-6),
-    codes = e4m3fn(y / scale). Returns (codes fp32-valued, dequant_scale [...,1] fp32)."""
+    codes = e4m3fn(y / scale) — or, with ``reciprocal``, e4m3fn(y * (1/scale)) in fp32 as the NKI
+    kernel computes it (adaln_quant.py:520-536). Returns (codes fp32-valued, dequant_scale [...,1] fp32)."""
     fp8_range = FP8_E4M3FN_MAX if ocp else FP8_E4M3_MAX
     yq = y
     amax = np.abs(yq).max(axis=-1, keepdims=True)
@@ -46,7 +47,11 @@ def row_quantize(y: np.ndarray, ocp: bool = True, lower_bound: float = 0.0):
         amax = np.clip(amax, a_min=None, a_max=lower_bound)
         yq = np.clip(yq, a_min=-lower_bound, a_max=lower_bound)
     dequant_scale = np.maximum(amax / fp8_range, MIN_DEQUANT_SCALE)
-    codes = e4m3fn_round(yq / dequant_scale)
+    if reciprocal:
+        inv = (np.float32(1.0) / dequant_scale.astype(np.float32)).astype(np.float32)
+        codes = e4m3fn_round((yq.astype(np.float32) * inv).astype(np.float32))
+    else:
+        codes = e4m3fn_round(yq / dequant_scale)
     return codes, dequant_scale.astype(np.float32)
 
 
@@ -164,7 +169,7 @@ def adaln_modulate_oracle(
     if quant == "none":
         out = bf16_round(y)
     elif quant == "row":
-        codes, scale = row_quantize(y, ocp=ocp)
+        codes, scale = row_quantize(y, ocp=ocp, reciprocal=True)
         out = pack_row(codes, scale)
     elif quant == "mx32":
         codes, scale_u8, _ = mx_quantize(y)

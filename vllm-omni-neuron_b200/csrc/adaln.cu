@@ -7,7 +7,7 @@
 //     xhat = LayerNorm(t) | RMSNorm(t) | t (fp32 statistics, two-pass mean/variance)
 //     y    = xhat * mul + add              (mul/add in bf16, arithmetic fp32)
 //     out  = bf16(y)                       (quant none)
-//          | e4m3fn(y / s), s = max(amax/range, 1e-6), packed [H codes | 4 bytes fp32 s]  (quant row)
+//          | e4m3fn(y * (1/s)), s = max(amax/range, 1e-6), packed [H codes | 4 bytes fp32 s] (quant row)
 //          | e4m3fn(y / 2^(e-127)), e = clip(max biased exponent of 32 values - 7, 0, 255)  (quant mx32)
 //
 // One 128-thread CTA per row; the row (<= 16384 values) stays in registers, 16-byte vector loads and
@@ -187,15 +187,15 @@ __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
   } else if (p.quant == 1) {
     amax = block_reduce<true>(amax, red);
     const float scale = fmaxf(amax / p.fp8_range, 1e-6f);
+    // codes = y * (1 / scale), the reciprocal-multiply of the reference kernel (adaln_quant.py:520-536)
+    const float inv = __frcp_rn(scale);
     uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * (p.packed ? H + 4 : H);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = threadIdx.x + i * kThreads;
       if (c >= nchunk) continue;
-      uint32_t w0 = e4m3x2(__fdiv_rn(x[i][0], scale), __fdiv_rn(x[i][1], scale)) |
-                    (static_cast<uint32_t>(e4m3x2(__fdiv_rn(x[i][2], scale), __fdiv_rn(x[i][3], scale))) << 16);
-      uint32_t w1 = e4m3x2(__fdiv_rn(x[i][4], scale), __fdiv_rn(x[i][5], scale)) |
-                    (static_cast<uint32_t>(e4m3x2(__fdiv_rn(x[i][6], scale), __fdiv_rn(x[i][7], scale))) << 16);
+      uint32_t w0 = e4m3x2(x[i][0] * inv, x[i][1] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][2] * inv, x[i][3] * inv)) << 16);
+      uint32_t w1 = e4m3x2(x[i][4] * inv, x[i][5] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][6] * inv, x[i][7] * inv)) << 16);
       if (p.packed) {  // rows are only 4-byte aligned (H + 4 bytes)
         reinterpret_cast<uint32_t*>(orow + c * 8)[0] = w0;
         reinterpret_cast<uint32_t*>(orow + c * 8)[1] = w1;

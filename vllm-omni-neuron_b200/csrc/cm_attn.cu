@@ -8,13 +8,15 @@
 // and partial results of different key ranges (ring steps) combine by plain addition; one final
 // normalise o_i = O_i / max(l_i, 1e-37).
 //
-// Kernel layout (one CTA = one 128-row query tile of one (batch, head)):
-//   warp 0      TMA producer: Q once, then K/V 128-key tiles into a 2-stage ring (no multicast)
-//   warp 1      TMEM owner + MMA issuer (one elected lane): S = Q K^T (SS form), O += P V (TS form,
-//               P read straight from TMEM)
-//   warps 2..5  softmax: one query row per thread (TMEM lane), P = exp2(S*scale*log2e - c*log2e)
-//               written back to TMEM as bf16, then the epilogue (normalise / partial write)
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+// Kernel layout (one CTA = two 128-row query tiles of one (batch, head)):
+//   warp 0      TMA producer: both Q tiles once, then K/V 128-key tiles into 2-stage rings (no multicast)
+//   warp 1      TMEM owner + MMA issuer (one elected lane): S_t = Q_t K^T (SS form), O_t += P_t V (TS
+//               form, P read straight from TMEM)
+//   warps 2..5  softmax of query tile 0, warps 6..9 of query tile 1: one query row per thread (TMEM
+//               lane), P = exp2(S*scale*log2e - c*log2e) written back to TMEM as bf16 over S, then
+//               the epilogue (normalise / partial write). The two warpgroups ping-pong: while one
+//               computes exponentials the tensor pipe runs the other tile's PV and next QK.
+// TMEM columns: S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -23,27 +25,31 @@
 #include "common.cuh"
 #include "host_util.h"
 
+#include <cstdlib>
 #include <mutex>
 
 namespace vomni {
 namespace cm {
 
-constexpr int kTile = 128;  // query rows per CTA and keys per tile
+constexpr int kTile = 128;  // query rows per tile and keys per tile
 constexpr int kD = 128;     // head dim (the reference asserts 128, ring_attention_const_max_fwd.py:1026)
-constexpr int kThreads = 192;
+constexpr int kQT = 2;      // query tiles per CTA (two softmax warpgroups ping-pong on the tensor pipe)
+constexpr int kThreads = 64 + 128 * kQT;
 constexpr uint32_t kTileBytes = kTile * kD * 2;  // 32 KB: one bf16 [128 x 128] tile
 constexpr uint32_t kHalfBytes = kTileBytes / 2;  // 16 KB: one [128 x 64] swizzled half
 
 // smem map (offsets from a 1024-aligned base)
-constexpr uint32_t kSmemQ = 0;
-constexpr uint32_t kSmemK = kSmemQ + kTileBytes;       // 2 stages
-constexpr uint32_t kSmemV = kSmemK + 2 * kTileBytes;   // 2 stages
+constexpr uint32_t kSmemQ = 0;                          // kQT tiles
+constexpr uint32_t kSmemK = kSmemQ + kQT * kTileBytes;  // 2 stages
+constexpr uint32_t kSmemV = kSmemK + 2 * kTileBytes;    // 2 stages
 constexpr uint32_t kSmemBar = kSmemV + 2 * kTileBytes;  // barriers + scalars
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + alignment slack
 
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 11, P_EMPTY = 13, O_FULL = 15, NBAR = 16 };
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 11, TURN = 13, O_FULL = 15, NBAR = 16 };
 
-constexpr uint32_t kColS = 0, kColO = 256, kColP = 384;
+// TMEM columns: tile t owns S_t = [t*128, t*128+128) (P_t, bf16, aliases its first 64 columns) and
+// O_t = [256 + t*128, 256 + t*128 + 128).
+constexpr uint32_t kColS = 0, kColO = 256;
 constexpr uint32_t kIdescQK = idesc_bf16(128, 128, false);
 constexpr uint32_t kIdescPV = idesc_bf16(128, 128, true);
 
@@ -64,6 +70,72 @@ struct Params {
   int* status;
 };
 
+// S = Q_t K^T: 8 MMAs of K=16 over the two 64-wide swizzled halves (K-major SW128: +32 B per step).
+__device__ __forceinline__ void issue_qk(uint32_t d_s, uint32_t q_addr, uint32_t k_addr) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+    mma_f16_ss(d_s, make_sdesc(q_addr + off, 16, 1024, kLayoutSW128), make_sdesc(k_addr + off, 16, 1024, kLayoutSW128),
+               kIdescQK, kk > 0);
+  }
+}
+// O_t += P_t V: P from TMEM (8 columns of packed bf16 per 16 keys), V as an MN-major SW128 operand
+// (16 keys = two 8-row groups = +2048 B; the two 64-wide d halves are 16 KB apart).
+__device__ __forceinline__ void issue_pv(uint32_t d_o, uint32_t p_tmem, uint32_t v_addr, bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    mma_f16_ts(d_o, p_tmem + kk * 8, make_sdesc(v_addr + kk * 2048, kHalfBytes, 1024, kLayoutSW128), kIdescPV,
+               (accumulate || kk > 0) ? 1u : 0u);
+}
+
+// One 32-column chunk of one query row: p = 2^(s*scale*log2e - c*log2e), summed into four
+// independent accumulators (no serial add chain) and packed to bf16 pairs for the PV MMA.
+// kPoly: every kPoly-th column goes through the FMA-pipe polynomial instead of the MUFU ex2 unit
+// (0 = none). kMask: columns at or past `valid` (keys outside this pass) contribute 0.
+template <int kPoly, bool kMask>
+VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], float scale_log2, float neg_c2, int valid, float (&acc)[4],
+                             uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float x0 = fmaf(__uint_as_float(s[2 * i]), scale_log2, neg_c2);
+    const float x1 = fmaf(__uint_as_float(s[2 * i + 1]), scale_log2, neg_c2);
+    float p0 = (kPoly > 0 && ((2 * i) % (kPoly > 0 ? kPoly : 1)) == kPoly - 1) ? exp2_poly(x0) : ex2_approx(x0);
+    float p1 = (kPoly > 0 && ((2 * i + 1) % (kPoly > 0 ? kPoly : 1)) == kPoly - 1) ? exp2_poly(x1) : ex2_approx(x1);
+    if (kMask) {
+      p0 = (2 * i < valid) ? p0 : 0.f;
+      p1 = (2 * i + 1 < valid) ? p1 : 0.f;
+    }
+    acc[i & 3] += p0 + p1;
+    pk[i] = pack_bf16x2(p0, p1);
+  }
+}
+
+template <int kPoly, bool kMask>
+VOMNI_DEV void softmax_tile(uint32_t col_s, float scale_log2, float neg_c2, int valid, float (&acc)[4]) {
+  // The whole 128-column S row is loaded with four back-to-back TMEM loads and one wait, so the
+  // TMEM latency is paid once per tile; P chunk ch then lands on columns [16ch, 16ch+16) of the
+  // same S region (all of it already read).
+  uint32_t s0[32], s1[32], s2[32], s3[32];
+  tmem_ld32(col_s, s0);
+  tmem_ld32(col_s + 32, s1);
+  tmem_ld32(col_s + 64, s2);
+  tmem_ld32(col_s + 96, s3);
+  tmem_ld_wait(s0);
+  tmem_ld_wait(s1);
+  tmem_ld_wait(s2);
+  tmem_ld_wait(s3);
+  uint32_t pk[16];
+  softmax_chunk<kPoly, kMask>(s0, scale_log2, neg_c2, valid, acc, pk);
+  tmem_st16(col_s, pk);
+  softmax_chunk<kPoly, kMask>(s1, scale_log2, neg_c2, valid - 32, acc, pk);
+  tmem_st16(col_s + 16, pk);
+  softmax_chunk<kPoly, kMask>(s2, scale_log2, neg_c2, valid - 64, acc, pk);
+  tmem_st16(col_s + 32, pk);
+  softmax_chunk<kPoly, kMask>(s3, scale_log2, neg_c2, valid - 96, acc, pk);
+  tmem_st16(col_s + 48, pk);
+}
+
+template <int kPoly, bool kPingPong>
 __global__ void __launch_bounds__(kThreads, 1)
     cm_attend_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -75,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_tile = blockIdx.x;
+  const int q0 = blockIdx.x * kTile * kQT;
   const int bh = blockIdx.y;
   const int b = bh / p.heads;
   const int h = bh % p.heads;
@@ -90,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars[V_EMPTY + i], 1);
       mbar_init(&bars[S_FULL + i], 1);
       mbar_init(&bars[P_FULL + i], 128);
-      mbar_init(&bars[P_EMPTY + i], 1);
+      mbar_init(&bars[TURN + i], 128);
     }
     mbar_init(&bars[O_FULL], 1);
     *abort_flag = 0;
@@ -115,11 +187,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      const int q_row = q_tile * kTile;
       const int x0 = h * kD;
-      mbar_expect_tx(&bars[Q_FULL], kTileBytes);
-      tma_load_3d(&tmQ, &bars[Q_FULL], sQ, x0, q_row, b);
-      tma_load_3d(&tmQ, &bars[Q_FULL], sQ + kHalfBytes, x0 + 64, q_row, b);
+      mbar_expect_tx(&bars[Q_FULL], kQT * kTileBytes);
+      for (int t = 0; t < kQT; ++t) {
+        tma_load_3d(&tmQ, &bars[Q_FULL], sQ + t * kTileBytes, x0, q0 + t * kTile, b);
+        tma_load_3d(&tmQ, &bars[Q_FULL], sQ + t * kTileBytes + kHalfBytes, x0 + 64, q0 + t * kTile, b);
+      }
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -136,56 +209,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Order per key tile j (tile t = 0, 1 alternating): PV_t(j-1) then QK_t(j). QK_t(j) overwrites
+    // S_t/P_t, which PV_t(j-1) reads; tcgen05.mma ops of one thread execute in issue order.
     if (lane == 0) {
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t k_addr = smem_u32(sK);
       const uint32_t v_addr = smem_u32(sV);
-      bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 3);
-      tc_fence_after();
-      for (int j = 0; ok && j <= n_tiles; ++j) {
-        if (j < n_tiles) {
-          const int st = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&bars[K_FULL + st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4)) break;
-          tc_fence_after();
-          const uint32_t d_s = tbase + kColS + st * 128;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            // K-major SW128: 16-element K step = +32 B inside a 128-B row; second 64-wide half at +16 KB.
-            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-            const uint64_t a = make_sdesc(q_addr + off, 16, 1024, kLayoutSW128);
-            const uint64_t bd = make_sdesc(k_addr + st * kTileBytes + off, 16, 1024, kLayoutSW128);
-            mma_f16_ss(d_s, a, bd, kIdescQK, kk > 0);
-          }
-          tc_commit(&bars[S_FULL + st]);
-          tc_commit(&bars[K_EMPTY + st]);
+      bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 3) &&
+                mbar_wait(&bars[K_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < kQT; ++t) {
+          issue_qk(tbase + kColS + t * 128, q_addr + t * kTileBytes, k_addr);
+          tc_commit(&bars[S_FULL + t]);
         }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const int bb = jj & 1;
-          const uint32_t ph = (jj >> 1) & 1;
-          if (!mbar_wait(&bars[P_FULL + bb], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) break;
-          if (!mbar_wait(&bars[V_FULL + bb], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) break;
+        tc_commit(&bars[K_EMPTY]);
+      }
+      for (int j = 1; ok && j <= n_tiles; ++j) {
+        const int jj = j - 1;
+        const int vs = jj & 1, ks = j & 1;
+        for (int t = 0; t < kQT && ok; ++t) {
+          if (!mbar_wait(&bars[P_FULL + t], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) { ok = false; break; }
+          if (t == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) { ok = false; break; }
           tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            // V is [keys][d] = MN-major B: 16 keys = two 8-row groups = +2048 B; d halves 16 KB apart (LBO).
-            const uint64_t bd = make_sdesc(v_addr + bb * kTileBytes + kk * 2048, kHalfBytes, 1024, kLayoutSW128);
-            mma_f16_ts(tbase + kColO, tbase + kColP + bb * 64 + kk * 8, bd, kIdescPV, (jj > 0 || kk > 0) ? 1u : 0u);
+          issue_pv(tbase + kColO + t * 128, tbase + kColS + t * 128, v_addr + vs * kTileBytes, jj > 0);
+          if (t == kQT - 1) tc_commit(&bars[V_EMPTY + vs]);
+          if (j < n_tiles) {
+            if (t == 0 && !mbar_wait(&bars[K_FULL + ks], (j >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk(tbase + kColS + t * 128, q_addr + t * kTileBytes, k_addr + ks * kTileBytes);
+            tc_commit(&bars[S_FULL + t]);
+            if (t == kQT - 1) tc_commit(&bars[K_EMPTY + ks]);
           }
-          tc_commit(&bars[V_EMPTY + bb]);
-          tc_commit(&bars[P_EMPTY + bb]);
         }
       }
       tc_commit(&bars[O_FULL]);
     }
   } else {
-    // ------------------------------------------------------------ softmax + epilogue (warps 2..5)
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
-    const int grow = q_tile * kTile + row;
+    const int grow = q0 + t * kTile + row;
     const bool row_ok = grow < p.s_q;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t col_s = tbase + lane_addr + kColS + t * 128;
+    const uint32_t col_o = tbase + lane_addr + kColO + t * 128;
     const size_t rowidx = static_cast<size_t>(bh) * p.s_q + grow;
     float c = 0.f;
     if (row_ok) {
@@ -195,38 +264,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       c = __bfloat162float(__float2bfloat16_rn(c32));
     }
     const float neg_c2 = -c * 1.4426950408889634f;
-    float rowsum = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const int bb = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait(&bars[S_FULL + bb], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
-      if (j >= 2 && !mbar_wait(&bars[P_EMPTY + bb], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 8)) { ok = false; break; }
+      if (!mbar_wait(&bars[S_FULL + t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+      // Ping-pong: tile 1's softmax of step j starts when tile 0's has finished it, and tile 0's
+      // softmax of step j waits for tile 1's of step j-1; each then runs while the tensor pipe does
+      // the other tile's PV and next QK, instead of both competing for the exp pipe at once.
+      if (kPingPong && t == 1 && !mbar_wait(&bars[TURN + 1], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 10)) { ok = false; break; }
+      if (kPingPong && t == 0 && j > 0 && !mbar_wait(&bars[TURN + 0], (j - 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 11)) { ok = false; break; }
       tc_fence_after();
       const int valid = p.n_keys - j * kTile;  // keys of this tile inside the pass's range
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t s[32];
-        tmem_ld32(tbase + lane_addr + kColS + bb * 128 + ch * 32, s);
-        tmem_ld_wait(s);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float p0 = ex2_approx(fmaf(__uint_as_float(s[2 * i]), p.scale_log2, neg_c2));
-          float p1 = ex2_approx(fmaf(__uint_as_float(s[2 * i + 1]), p.scale_log2, neg_c2));
-          if (valid < kTile) {
-            if (ch * 32 + 2 * i >= valid) p0 = 0.f;
-            if (ch * 32 + 2 * i + 1 >= valid) p1 = 0.f;
-          }
-          rowsum += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(tbase + lane_addr + kColP + bb * 64 + ch * 16, pk);
-      }
+      if (valid >= kTile)
+        softmax_tile<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc);
+      else
+        softmax_tile<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars[P_FULL + bb]);
+      mbar_arrive(&bars[P_FULL + t]);
+      if (kPingPong) mbar_arrive(&bars[TURN + (t ^ 1)]);
     }
+    const float rowsum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     // ---------------------------------------------------------- epilogue
     if (ok && mbar_wait(&bars[O_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) {
       tc_fence_after();
@@ -239,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         uint32_t o[32];
-        tmem_ld32(tbase + lane_addr + kColO + ch * 32, o);
+        tmem_ld32(col_o + ch * 32, o);
         tmem_ld_wait(o);
         if (!row_ok) continue;
         float v[32];
@@ -416,13 +474,23 @@ extern "C" int vomni_cm_attend(const void* q, const void* k, const void* v, int 
   p.flags = flags;
   p.status = device_status_ptr();
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(cm::cm_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kSmemBytes));
-    attr_set = true;
+  // Tuning knobs (read once): VOMNI_CM_POLY = share of exponentials on the FMA pipe as 1/N
+  // (0 = none), VOMNI_CM_PINGPONG = 0/1.
+  static int poly = -1, pingpong = -1;
+  if (poly < 0) {
+    const char* e = getenv("VOMNI_CM_POLY");
+    poly = e ? atoi(e) : 0;
+    const char* f = getenv("VOMNI_CM_PINGPONG");
+    pingpong = f ? atoi(f) : 1;
   }
-  dim3 grid((s_q + cm::kTile - 1) / cm::kTile, b * h);
-  cm::cm_attend_kernel<<<grid, cm::kThreads, cm::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  auto kern = cm::cm_attend_kernel<0, true>;
+  if (poly == 2) kern = pingpong ? cm::cm_attend_kernel<2, true> : cm::cm_attend_kernel<2, false>;
+  else if (poly == 4) kern = pingpong ? cm::cm_attend_kernel<4, true> : cm::cm_attend_kernel<4, false>;
+  else if (poly == 8) kern = pingpong ? cm::cm_attend_kernel<8, true> : cm::cm_attend_kernel<8, false>;
+  else kern = pingpong ? cm::cm_attend_kernel<0, true> : cm::cm_attend_kernel<0, false>;
+  VOMNI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kSmemBytes));
+  dim3 grid((s_q + cm::kTile * cm::kQT - 1) / (cm::kTile * cm::kQT), b * h);
+  kern<<<grid, cm::kThreads, cm::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }

@@ -52,15 +52,26 @@ VOMNI_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes (or
+// the hint elapses) instead of spinning, so waiting producer / MMA / softmax threads do not take
+// issue slots from the warps doing the math.
+VOMNI_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with parity `parity` of `bar` has completed. Returns false (and raises
 // `*abort`) when the budget runs out or another thread of the CTA already aborted.
 VOMNI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > kWaitBudgetNs) {
       *abort = 1;
@@ -144,7 +155,9 @@ VOMNI_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 // Completes the preceding tcgen05.ld; the registers are threaded through so no use of them can be
-// scheduled above the wait.
+// scheduled above the wait. tcgen05.ld / tcgen05.st carry no "memory" clobber (they touch only
+// TMEM and registers), so independent math can be scheduled across them; their order against
+// each other (both asm volatile) and against the barrier fences (which do clobber memory) stays.
 VOMNI_DEV void tmem_ld_wait(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
@@ -160,8 +173,7 @@ VOMNI_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
       "%16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
 VOMNI_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -193,6 +205,23 @@ VOMNI_DEV float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+// 2^x on the FMA pipe, for x <= 0 (softmax exponents under a fixed upper bound). Cody-Waite split
+// x = n + f with n = rint(x) (added to 1.5 * 2^23 so n lands in the low mantissa bits) and
+// f in [-0.5, 0.5]; 2^f from a degree-3 polynomial whose coefficients come from a Remez exchange
+// minimising the relative error on [-0.5, 0.5] (max 7.5e-5, i.e. 2^-13.7, far below the bf16
+// rounding the result gets); 2^n is then added into the exponent field. x is clamped at -125 so
+// the exponent never underflows: inputs below give 2^-125 (~2.4e-38) instead of 0.
+VOMNI_DEV float exp2_poly(float x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  x = fmaxf(x, -125.f);
+  const float t = x + kRound;
+  const float f = x - (t - kRound);
+  float p = fmaf(0.0551716685f, f, 0.2426111251f);
+  p = fmaf(p, f, 0.6932609677f);
+  p = fmaf(p, f, 0.9999280572f);
+  // (bits(t) - bits(kRound)) << 23 == bits(t) << 23 (mod 2^32): bits(kRound) has 23 zero low bits.
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 // Two fp32 -> packed bf16x2 (round to nearest even); `lo` lands in bits 0-15.
 VOMNI_DEV uint32_t pack_bf16x2(float lo, float hi) {
