@@ -71,21 +71,21 @@ struct Params {
 };
 
 // S = Q_t K^T: 8 MMAs of K=16 over the two 64-wide swizzled halves (K-major SW128: +32 B per step).
-__device__ __forceinline__ void issue_qk(uint32_t d_s, uint32_t q_addr, uint32_t k_addr) {
+// Descriptors are built once per CTA; the start-address field (bits 0-13, address >> 4) is then
+// advanced by plain integer adds (no carry: shared addresses stay below 256 KB).
+__device__ __forceinline__ void issue_qk(uint32_t d_s, uint64_t q_desc, uint64_t k_desc) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-    mma_f16_ss(d_s, make_sdesc(q_addr + off, 16, 1024, kLayoutSW128), make_sdesc(k_addr + off, 16, 1024, kLayoutSW128),
-               kIdescQK, kk > 0);
+    const uint64_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+    mma_f16_ss(d_s, q_desc + off, k_desc + off, kIdescQK, kk > 0);
   }
 }
 // O_t += P_t V: P from TMEM (8 columns of packed bf16 per 16 keys), V as an MN-major SW128 operand
 // (16 keys = two 8-row groups = +2048 B; the two 64-wide d halves are 16 KB apart).
-__device__ __forceinline__ void issue_pv(uint32_t d_o, uint32_t p_tmem, uint32_t v_addr, bool accumulate) {
+__device__ __forceinline__ void issue_pv(uint32_t d_o, uint32_t p_tmem, uint64_t v_desc, bool accumulate) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    mma_f16_ts(d_o, p_tmem + kk * 8, make_sdesc(v_addr + kk * 2048, kHalfBytes, 1024, kLayoutSW128), kIdescPV,
-               (accumulate || kk > 0) ? 1u : 0u);
+    mma_f16_ts(d_o, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV, (accumulate || kk > 0) ? 1u : 0u);
 }
 
 // One 32-column chunk of one query row: p = 2^(s*scale*log2e - c*log2e), summed into four
@@ -212,15 +212,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Order per key tile j (tile t = 0, 1 alternating): PV_t(j-1) then QK_t(j). QK_t(j) overwrites
     // S_t/P_t, which PV_t(j-1) reads; tcgen05.mma ops of one thread execute in issue order.
     if (lane == 0) {
-      const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t k_addr = smem_u32(sK);
-      const uint32_t v_addr = smem_u32(sV);
+      const uint64_t q_desc = make_sdesc(smem_u32(sQ), 16, 1024, kLayoutSW128);
+      const uint64_t k_desc = make_sdesc(smem_u32(sK), 16, 1024, kLayoutSW128);
+      const uint64_t v_desc = make_sdesc(smem_u32(sV), kHalfBytes, 1024, kLayoutSW128);
+      constexpr uint64_t kTileDesc = kTileBytes >> 4;
       bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 3) &&
                 mbar_wait(&bars[K_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < kQT; ++t) {
-          issue_qk(tbase + kColS + t * 128, q_addr + t * kTileBytes, k_addr);
+          issue_qk(tbase + kColS + t * 128, q_desc + t * kTileDesc, k_desc);
           tc_commit(&bars[S_FULL + t]);
         }
         tc_commit(&bars[K_EMPTY]);
@@ -232,12 +233,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&bars[P_FULL + t], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) { ok = false; break; }
           if (t == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(tbase + kColO + t * 128, tbase + kColS + t * 128, v_addr + vs * kTileBytes, jj > 0);
+          issue_pv(tbase + kColO + t * 128, tbase + kColS + t * 128, v_desc + vs * kTileDesc, jj > 0);
           if (t == kQT - 1) tc_commit(&bars[V_EMPTY + vs]);
           if (j < n_tiles) {
             if (t == 0 && !mbar_wait(&bars[K_FULL + ks], (j >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4)) { ok = false; break; }
             tc_fence_after();
-            issue_qk(tbase + kColS + t * 128, q_addr + t * kTileBytes, k_addr + ks * kTileBytes);
+            issue_qk(tbase + kColS + t * 128, q_desc + t * kTileDesc, k_desc + ks * kTileDesc);
             tc_commit(&bars[S_FULL + t]);
             if (t == kQT - 1) tc_commit(&bars[K_EMPTY + ks]);
           }
@@ -481,7 +482,7 @@ extern "C" int vomni_cm_attend(const void* q, const void* k, const void* v, int 
     const char* e = getenv("VOMNI_CM_POLY");
     poly = e ? atoi(e) : 0;
     const char* f = getenv("VOMNI_CM_PINGPONG");
-    pingpong = f ? atoi(f) : 1;
+    pingpong = f ? atoi(f) : 0;
   }
   auto kern = cm::cm_attend_kernel<0, true>;
   if (poly == 2) kern = pingpong ? cm::cm_attend_kernel<2, true> : cm::cm_attend_kernel<2, false>;

@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = true;
+      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128);
       for (int kb = 0; kb < nk; ++kb) {
         const int st = kb % kStages;
         const uint32_t ph = (kb / kStages) & 1;
@@ -106,14 +107,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + st * kStageBytes);
-        const uint32_t b_addr = a_addr + kABytes;
+        // Start-address field advanced by integer adds (address >> 4; no carry below 256 KB).
+        const uint64_t ad0 = a_desc0 + ((st * kStageBytes) >> 4);
+        const uint64_t bd0 = ad0 + (kABytes >> 4);
 #pragma unroll
-        for (int k4 = 0; k4 < kBK / 32; ++k4) {
-          const uint64_t ad = make_sdesc(a_addr + k4 * 32, 16, 1024, kLayoutSW128);
-          const uint64_t bd = make_sdesc(b_addr + k4 * 32, 16, 1024, kLayoutSW128);
-          mma_f8_ss(tacc, ad, bd, kIdesc, (kb > 0 || k4 > 0) ? 1u : 0u);
-        }
+        for (int k4 = 0; k4 < kBK / 32; ++k4)
+          mma_f8_ss(tacc, ad0 + k4 * 2, bd0 + k4 * 2, kIdesc, (kb > 0 || k4 > 0) ? 1u : 0u);
         tc_commit(&empty[st]);
       }
       if (ok) tc_commit(acc_full);
