@@ -11,11 +11,11 @@
 //          out = x*inv*cos + [-x_hi, x_lo]*inv*sin                  (_rope_segment, :4069-4114)
 // The MX engine's identity micro-scales (common_types.py:77-78) make the ROW mode a plain FP8 GEMM.
 //
-// GEMM kernel: one CTA = one 128 x 256 output tile; warp 0 TMA producer (A [128 x 128 B] and
-// B [256 x 128 B] boxes, 128-byte swizzle, 2-stage ring), warp 1 TMEM owner + tcgen05.mma
-// kind::f8f6f4 issuer (M=128, N=256, K=32 per instruction), warps 2-5 epilogue (TMEM -> registers,
-// scales + bias, bf16 stores, per-row partial sums of squares). 2 CTAs per SM overlap one CTA's
-// epilogue with the other's main loop.
+// GEMM kernel: persistent, one CTA per SM walking 128 x 256 output tiles; warp 0 TMA producer
+// (A [128 x 128 B] and B [256 x 128 B] boxes, 128-byte swizzle, 4-stage ring), warp 1 TMEM owner +
+// tcgen05.mma kind::f8f6f4 issuer (M=128, N=256, K=32 per instruction) into one of two 256-column
+// accumulators, warps 2-5 epilogue (TMEM -> registers, scales + bias, bf16 stores, per-row partial
+// sums of squares) on the other accumulator.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -27,17 +27,18 @@ namespace vomni {
 namespace qkv {
 
 constexpr int kBM = 128, kBN = 256, kBK = 128;  // kBK in bytes (= fp8 elements)
-constexpr int kStages = 2;
+constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t kABytes = kBM * kBK;  // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK;  // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kSmemBar = kStages * kStageBytes;
-constexpr uint32_t kSmemBytes = kSmemBar + 128 + 1024;
+constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;
 constexpr uint32_t kIdesc = idesc_e4m3(kBM, kBN);
 
 struct Params {
   int T, I, H;
+  int m_tiles, n_tiles;
   const float* row_scale;   // [T]
   const float* chan_scale;  // [I]
   const __nv_bfloat16* bias;  // [I] or null
@@ -47,91 +48,120 @@ struct Params {
   int* status;
 };
 
-__global__ void __launch_bounds__(kThreads, 2)
+// Persistent: CTA c processes tiles c, c + gridDim.x, ... (n fastest, so the CTAs in flight share
+// the A rows and walk the whole weight, which stays L2-resident). The two 256-column TMEM
+// accumulators alternate between tiles, so the epilogue of tile i overlaps the main loop of i+1.
+__global__ void __launch_bounds__(kThreads, 1)
     qkv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + kStages;   // [2]
+  uint64_t* acc_empty = acc_full + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM;
-  const int nt = blockIdx.y;
-  const int n0 = nt * kBN;
   const int nk = p.H / kBK;
+  const int n_all = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kBN);
+    tmem_alloc(tmem_slot, 2 * kBN);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tacc = *tmem_slot;
+  const uint32_t tbase = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int st = kb % kStages;
-        const uint32_t ph = (kb / kStages) & 1;
-        if (kb >= kStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) break;
-        uint8_t* sa = smem + st * kStageBytes;
-        mbar_expect_tx(&full[st], kStageBytes);
-        tma_load_2d(&tmA, &full[st], sa, kb * kBK, m0);
-        tma_load_2d(&tmB, &full[st], sa + kABytes, kb * kBK, n0);
+      uint32_t it = 0;  // global k-block counter across this CTA's tiles (stage ring position)
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x) {
+        const int m0 = (tile / p.n_tiles) * kBM;
+        const int n0 = (tile % p.n_tiles) * kBN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (it >= kStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * kStageBytes;
+          mbar_expect_tx(&full[st], kStageBytes);
+          tma_load_2d(&tmA, &full[st], sa, kb * kBK, m0);
+          tma_load_2d(&tmB, &full[st], sa + kABytes, kb * kBK, n0);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      bool ok = true;
       const uint64_t a_desc0 = make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int st = kb % kStages;
-        const uint32_t ph = (kb / kStages) & 1;
-        if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x22)) {
-          ok = false;
-          break;
-        }
+      uint32_t it = 0;
+      int lt = 0;  // local tile index
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[acc], ((lt >> 1) & 1) ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24)) break;
         tc_fence_after();
-        // Start-address field advanced by integer adds (address >> 4; no carry below 256 KB).
-        const uint64_t ad0 = a_desc0 + ((st * kStageBytes) >> 4);
-        const uint64_t bd0 = ad0 + (kABytes >> 4);
+        const uint32_t tacc = tbase + acc * kBN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x22)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // Start-address field advanced by integer adds (address >> 4; no carry below 256 KB).
+          const uint64_t ad0 = a_desc0 + ((st * kStageBytes) >> 4);
+          const uint64_t bd0 = ad0 + (kABytes >> 4);
 #pragma unroll
-        for (int k4 = 0; k4 < kBK / 32; ++k4)
-          mma_f8_ss(tacc, ad0 + k4 * 2, bd0 + k4 * 2, kIdesc, (kb > 0 || k4 > 0) ? 1u : 0u);
-        tc_commit(&empty[st]);
+          for (int k4 = 0; k4 < kBK / 32; ++k4)
+            mma_f8_ss(tacc, ad0 + k4 * 2, bd0 + k4 * 2, kIdesc, (kb > 0 || k4 > 0) ? 1u : 0u);
+          tc_commit(&empty[st]);
+        }
+        if (ok) tc_commit(&acc_full[acc]);
       }
-      if (ok) tc_commit(acc_full);
     }
   } else {
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const int grow = m0 + row;
-    const bool row_ok = grow < p.T;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    if (mbar_wait(acc_full, 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x23)) {
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < n_all; tile += gridDim.x, ++lt) {
+      const int acc = lt & 1;
+      if (!mbar_wait(&acc_full[acc], (lt >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x23)) break;
       tc_fence_after();
+      const int m0 = (tile / p.n_tiles) * kBM;
+      const int nt = tile % p.n_tiles;
+      const int n0 = nt * kBN;
+      const int grow = m0 + row;
+      const bool row_ok = grow < p.T;
+      const uint32_t tacc = tbase + lane_addr + acc * kBN;
       const float rs = row_ok ? p.row_scale[grow] : 0.f;
       float ss = 0.f;
       __nv_bfloat16* yrow = p.y + static_cast<size_t>(grow) * p.I + n0;
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tacc + lane_addr + c * 32, r);
+        tmem_ld32(tacc + c * 32, r);
         tmem_ld_wait(r);
         const int col0 = n0 + c * 32;
         const float4* cs4 = reinterpret_cast<const float4*>(p.chan_scale + col0);
@@ -171,6 +201,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
+      // The accumulator has been read: the MMA warp may reuse it for tile lt + 2.
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
       if (row_ok && p.sumsq && nt < p.n_norm_tiles) p.sumsq[static_cast<size_t>(grow) * p.n_norm_tiles + nt] = ss;
     }
   }
@@ -178,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tacc, kBN);
+    tmem_dealloc(tbase, 2 * kBN);
   }
 }
 
@@ -322,13 +355,16 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
   p.y = static_cast<__nv_bfloat16*>(y);
   p.sumsq = sumsq;
   p.n_norm_tiles = (q_dim + kv_dim) / qkv::kBN;
+  p.m_tiles = (t + qkv::kBM - 1) / qkv::kBM;
+  p.n_tiles = i / qkv::kBN;
   p.status = device_status_ptr();
   static bool attr = false;
   if (!attr) {
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kSmemBytes));
     attr = true;
   }
-  dim3 grid((t + qkv::kBM - 1) / qkv::kBM, i / qkv::kBN);
+  const int n_all = p.m_tiles * p.n_tiles;
+  const int grid = n_all < num_sms() ? n_all : num_sms();
   qkv::qkv_gemm_kernel<<<grid, qkv::kThreads, qkv::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
