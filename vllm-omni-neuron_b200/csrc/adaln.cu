@@ -94,155 +94,195 @@ __device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
 }
 
 // NV = 16-byte chunks (8 values) per thread; a row holds up to NV * 128 * 8 values.
-template <int NV>
+// Persistent: CTA c handles rows c, c + gridDim.x, ...; the next row's hidden (and residual) chunks
+// are loaded before the current row's reductions, and the modulation vectors stay in registers
+// for as long as consecutive rows share them.
+template <int NV, bool kRes>
 __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
   __shared__ float red[kWarps];
-  const long long row = blockIdx.x;
-  if (row >= p.rows) return;
   const int H = p.H;
   const int nchunk = H >> 3;
-  const long long mrow = row / p.rows_per_mod;
-  const size_t base = static_cast<size_t>(row) * H;
+  long long row = blockIdx.x;
+  if (row >= p.rows) return;
 
-  float x[NV][8];
-  // ---- load + gated residual
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = threadIdx.x + i * kThreads;
-    if (c < nchunk) {
-      unpack8(reinterpret_cast<const uint4*>(p.hidden + base)[c], x[i]);
-      if (p.residual) {
-        float r[8];
-        unpack8(reinterpret_cast<const uint4*>(p.residual + base)[c], r);
-        if (p.gate) {
-          const float4* g = reinterpret_cast<const float4*>(p.gate + static_cast<size_t>(mrow) * H + c * 8);
-          const float4 g0 = g[0], g1 = g[1];
-          x[i][0] *= g0.x; x[i][1] *= g0.y; x[i][2] *= g0.z; x[i][3] *= g0.w;
-          x[i][4] *= g1.x; x[i][5] *= g1.y; x[i][6] *= g1.z; x[i][7] *= g1.w;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) x[i][j] = __bfloat162float(__float2bfloat16_rn(r[j] + x[i][j]));
-        reinterpret_cast<uint4*>(p.residual_out + base)[c] = pack8(x[i]);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
-    }
-  }
-  // ---- statistics (fp32, two-pass for LayerNorm)
-  const float invH = 1.f / static_cast<float>(H);
-  float mean = 0.f, rstd = 1.f;
-  if (p.norm == 0) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) s += x[i][j];
-    mean = block_reduce<false>(s, red) * invH;
-    float v = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      if (threadIdx.x + i * kThreads < nchunk) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float d = x[i][j] - mean;
-          v = fmaf(d, d, v);
-        }
-      }
-    }
-    rstd = rsqrtf(block_reduce<false>(v, red) * invH + p.eps);
-  } else if (p.norm == 1) {
-    float v = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v = fmaf(x[i][j], x[i][j], v);
-    rstd = rsqrtf(block_reduce<false>(v, red) * invH + p.eps);
-  }
-  // ---- normalise + modulate
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = threadIdx.x + i * kThreads;
-    if (c >= nchunk) continue;
-    float m[8], a[8];
-    if (p.mul) unpack8(reinterpret_cast<const uint4*>(p.mul + static_cast<size_t>(mrow) * H)[c], m);
-    if (p.add) unpack8(reinterpret_cast<const uint4*>(p.add + static_cast<size_t>(mrow) * H)[c], a);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float y = p.norm == 2 ? x[i][j] : (x[i][j] - mean) * rstd;
-      if (p.mul) y *= m[j];
-      if (p.add) y += a[j];
-      x[i][j] = y;
-      amax = fmaxf(amax, fabsf(y));
-    }
-  }
-  // ---- quantise + store
-  if (p.quant == 0) {
+  uint4 hn[NV], rn[NV];  // next row, raw bf16
+  auto load_row = [&](long long r) {
+    const uint4* hp = reinterpret_cast<const uint4*>(p.hidden + static_cast<size_t>(r) * H);
+    const uint4* rp = kRes ? reinterpret_cast<const uint4*>(p.residual + static_cast<size_t>(r) * H) : nullptr;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = threadIdx.x + i * kThreads;
-      if (c < nchunk) reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base)[c] = pack8(x[i]);
-    }
-  } else if (p.quant == 1) {
-    amax = block_reduce<true>(amax, red);
-    const float scale = fmaxf(amax / p.fp8_range, 1e-6f);
-    // codes = y * (1 / scale), the reciprocal-multiply of the reference kernel (adaln_quant.py:520-536)
-    const float inv = __frcp_rn(scale);
-    uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * (p.packed ? H + 4 : H);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = threadIdx.x + i * kThreads;
-      if (c >= nchunk) continue;
-      uint32_t w0 = e4m3x2(x[i][0] * inv, x[i][1] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][2] * inv, x[i][3] * inv)) << 16);
-      uint32_t w1 = e4m3x2(x[i][4] * inv, x[i][5] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][6] * inv, x[i][7] * inv)) << 16);
-      if (p.packed) {  // rows are only 4-byte aligned (H + 4 bytes)
-        reinterpret_cast<uint32_t*>(orow + c * 8)[0] = w0;
-        reinterpret_cast<uint32_t*>(orow + c * 8)[1] = w1;
-      } else {
-        reinterpret_cast<uint2*>(orow)[c] = make_uint2(w0, w1);
-      }
-    }
-    if (threadIdx.x == 0) {
-      if (p.packed)
-        *reinterpret_cast<float*>(orow + H) = scale;
-      else
-        static_cast<float*>(p.out_scale)[row] = scale;
-    }
-  } else {  // mx32: a 32-value block = 4 consecutive chunks = 4 consecutive threads of one i
-    uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * H;
-    uint8_t* srow = static_cast<uint8_t*>(p.out_scale) + static_cast<size_t>(row) * (H >> 5);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = threadIdx.x + i * kThreads;
-      int e = 0;
       if (c < nchunk) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) e = max(e, static_cast<int>((__float_as_uint(x[i][j]) >> 23) & 0xFF));
+        hn[i] = __ldcs(hp + c);  // streamed once: evict-first
+        if (kRes) rn[i] = __ldcs(rp + c);
       }
-      e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
-      e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
-      if (c >= nchunk) continue;
-      const int su = min(max(e - 7, 0), 255);
-      // y / 2^(su - 127) as two exact power-of-two multiplies (each factor a normal fp32).
-      const int sh = 127 - su;  // in [-128, 127]
-      const int sa = sh / 2, sb = sh - sa;
-      const float fa = __uint_as_float(static_cast<uint32_t>(sa + 127) << 23);
-      const float fb = __uint_as_float(static_cast<uint32_t>(sb + 127) << 23);
-      float q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = fminf(fmaxf((x[i][j] * fa) * fb, -448.f), 448.f);
-      const uint32_t w0 = e4m3x2(q[0], q[1]) | (static_cast<uint32_t>(e4m3x2(q[2], q[3])) << 16);
-      const uint32_t w1 = e4m3x2(q[4], q[5]) | (static_cast<uint32_t>(e4m3x2(q[6], q[7])) << 16);
-      reinterpret_cast<uint2*>(orow)[c] = make_uint2(w0, w1);
-      if ((c & 3) == 0) srow[c >> 2] = static_cast<uint8_t>(su);
     }
+  };
+  load_row(row);
+  long long cached_mrow = -1;
+  uint4 mul_r[NV], add_r[NV];
+  const uint4 one_bf16x8 = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+
+  while (row < p.rows) {
+    const long long next = row + gridDim.x;
+    const size_t base = static_cast<size_t>(row) * H;
+    const long long mrow = row / p.rows_per_mod;
+    float x[NV][8];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      unpack8(hn[i], x[i]);
+      if (kRes) {
+        const int c = threadIdx.x + i * kThreads;
+        float r[8];
+        unpack8(rn[i], r);
+        if (c < nchunk) {
+          if (p.gate) {
+            const float4* g = reinterpret_cast<const float4*>(p.gate + static_cast<size_t>(mrow) * H + c * 8);
+            const float4 g0 = g[0], g1 = g[1];
+            x[i][0] *= g0.x; x[i][1] *= g0.y; x[i][2] *= g0.z; x[i][3] *= g0.w;
+            x[i][4] *= g1.x; x[i][5] *= g1.y; x[i][6] *= g1.z; x[i][7] *= g1.w;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[i][j] = __bfloat162float(__float2bfloat16_rn(r[j] + x[i][j]));
+          reinterpret_cast<uint4*>(p.residual_out + base)[c] = pack8(x[i]);
+        }
+      }
+      if (threadIdx.x + i * kThreads >= nchunk) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
+      }
+    }
+    if (next < p.rows) load_row(next);  // overlaps this row's reductions and stores
+    if (mrow != cached_mrow) {
+      cached_mrow = mrow;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = threadIdx.x + i * kThreads;
+        mul_r[i] = (p.mul && c < nchunk) ? reinterpret_cast<const uint4*>(p.mul + static_cast<size_t>(mrow) * H)[c] : one_bf16x8;
+        add_r[i] = (p.add && c < nchunk) ? reinterpret_cast<const uint4*>(p.add + static_cast<size_t>(mrow) * H)[c] : make_uint4(0, 0, 0, 0);
+      }
+    }
+    // ---- statistics (fp32, two-pass for LayerNorm)
+    const float invH = 1.f / static_cast<float>(H);
+    float mean = 0.f, rstd = 1.f;
+    if (p.norm == 0) {
+      float sm = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sm += x[i][j];
+      mean = block_reduce<false>(sm, red) * invH;
+      float v = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (threadIdx.x + i * kThreads < nchunk) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float d = x[i][j] - mean;
+            v = fmaf(d, d, v);
+          }
+        }
+      }
+      rstd = rsqrtf(block_reduce<false>(v, red) * invH + p.eps);
+    } else if (p.norm == 1) {
+      float v = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v = fmaf(x[i][j], x[i][j], v);
+      rstd = rsqrtf(block_reduce<false>(v, red) * invH + p.eps);
+    }
+    // ---- normalise + modulate (mul defaults to 1, add to 0)
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float m[8], a[8];
+      unpack8(mul_r[i], m);
+      unpack8(add_r[i], a);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float y = p.norm == 2 ? x[i][j] : (x[i][j] - mean) * rstd;
+        y = fmaf(y, m[j], a[j]);
+        x[i][j] = y;
+        amax = fmaxf(amax, fabsf(y));
+      }
+    }
+    // ---- quantise + store
+    if (p.quant == 0) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = threadIdx.x + i * kThreads;
+        if (c < nchunk) __stcs(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base) + c, pack8(x[i]));
+      }
+    } else if (p.quant == 1) {
+      amax = block_reduce<true>(amax, red);
+      const float scale = fmaxf(amax / p.fp8_range, 1e-6f);
+      // codes = y * (1 / scale), the reciprocal-multiply of the reference kernel (adaln_quant.py:520-536)
+      const float inv = __frcp_rn(scale);
+      uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * (p.packed ? H + 4 : H);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = threadIdx.x + i * kThreads;
+        if (c >= nchunk) continue;
+        const uint32_t w0 = e4m3x2(x[i][0] * inv, x[i][1] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][2] * inv, x[i][3] * inv)) << 16);
+        const uint32_t w1 = e4m3x2(x[i][4] * inv, x[i][5] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][6] * inv, x[i][7] * inv)) << 16);
+        if (p.packed) {  // rows are only 4-byte aligned (H + 4 bytes)
+          reinterpret_cast<uint32_t*>(orow + c * 8)[0] = w0;
+          reinterpret_cast<uint32_t*>(orow + c * 8)[1] = w1;
+        } else {
+          __stcs(reinterpret_cast<uint2*>(orow) + c, make_uint2(w0, w1));
+        }
+      }
+      if (threadIdx.x == 0) {
+        if (p.packed)
+          *reinterpret_cast<float*>(orow + H) = scale;
+        else
+          static_cast<float*>(p.out_scale)[row] = scale;
+      }
+    } else {  // mx32: a 32-value block = 4 consecutive chunks = 4 consecutive threads of one i
+      uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * H;
+      uint8_t* srow = static_cast<uint8_t*>(p.out_scale) + static_cast<size_t>(row) * (H >> 5);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = threadIdx.x + i * kThreads;
+        int e = 0;
+        if (c < nchunk) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) e = max(e, static_cast<int>((__float_as_uint(x[i][j]) >> 23) & 0xFF));
+        }
+        e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
+        e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
+        if (c >= nchunk) continue;
+        const int su = min(max(e - 7, 0), 255);
+        // y / 2^(su - 127) as two exact power-of-two multiplies (each factor a normal fp32).
+        const int sh = 127 - su;  // in [-128, 127]
+        const int sa = sh / 2, sb = sh - sa;
+        const float fa = __uint_as_float(static_cast<uint32_t>(sa + 127) << 23);
+        const float fb = __uint_as_float(static_cast<uint32_t>(sb + 127) << 23);
+        float q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = fminf(fmaxf((x[i][j] * fa) * fb, -448.f), 448.f);
+        const uint32_t w0 = e4m3x2(q[0], q[1]) | (static_cast<uint32_t>(e4m3x2(q[2], q[3])) << 16);
+        const uint32_t w1 = e4m3x2(q[4], q[5]) | (static_cast<uint32_t>(e4m3x2(q[6], q[7])) << 16);
+        reinterpret_cast<uint2*>(orow)[c] = make_uint2(w0, w1);
+        if ((c & 3) == 0) srow[c >> 2] = static_cast<uint8_t>(su);
+      }
+    }
+    row = next;
   }
 }
 
 template <int NV>
 int launch(const Params& p, cudaStream_t st) {
-  adaln_kernel<NV><<<static_cast<unsigned>(p.rows), kThreads, 0, st>>>(p);
+  // Persistent grid: as many CTAs as fit on the device at once, each walking rows with a one-row
+  // prefetch.
+  auto kern = p.residual ? adaln_kernel<NV, true> : adaln_kernel<NV, false>;
+  int per_sm = 0;
+  VOMNI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0));
+  if (per_sm < 1) per_sm = 1;
+  const long long cap = static_cast<long long>(num_sms()) * per_sm;
+  const unsigned grid = static_cast<unsigned>(p.rows < cap ? p.rows : cap);
+  kern<<<grid, kThreads, 0, st>>>(p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }
