@@ -52,6 +52,13 @@ VOMNI_API const char* vomni_strerror(int code);
 /* Synchronises the device, copies the status word to *code, optionally clears it. */
 VOMNI_API int vomni_device_status(int* code, int clear);
 
+/* Failure-detection self-test (no counterpart in the reference, whose kernels have no runtime
+ * waits): one CTA waits on an mbarrier that nothing arrives on, with a budget of budget_us
+ * microseconds (<= 2 s). The bounded wait gives up, the kernel ends normally, the device status
+ * word reads VOMNI_DEV_TIMEOUT_BASE + 0x7F and *result_host = 0 (1 would mean the wait
+ * completed). Synchronises `stream`. */
+VOMNI_API int vomni_selftest_bounded_wait(unsigned budget_us, int* result_host, vomni_stream_t stream);
+
 /* ------------------------------------------------------------------ const-max attention
  * Replaces the NKI kernel ring_attention_const_max_fwd
  * (vllm_omni_neuron/kernels/nkilib/experimental/attention/ring_attention_const_max_fwd.py:958-1404)
@@ -85,6 +92,20 @@ VOMNI_API int vomni_cm_prologue(const void* q, const void* k, int b, int s, int 
 VOMNI_API int vomni_cm_attend(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start, int n_keys,
                     int h, int d, float softmax_scale, const float* qn2, const float* kmax2, float* acc_o,
                     float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream);
+
+/* Strided forms: q and k/v rows (tokens) are q_stride / kv_stride elements apart (0 = dense h*d;
+ * >= h*d, multiple of 8), batch stride s * stride — the token-major views a fused [b, s, 3*h*d]
+ * QKV projection hands out (row_mx_modules.py:390-393 tensor_split), read without a copy. */
+VOMNI_API int vomni_cm_prologue_strided(const void* q, const void* k, int b, int s, int h, int d, long long q_stride,
+                                        long long k_stride, float* qn2, float* kmax2, vomni_stream_t stream);
+VOMNI_API int vomni_cm_attend_strided(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start,
+                                      int n_keys, int h, int d, long long q_stride, long long kv_stride,
+                                      float softmax_scale, const float* qn2, const float* kmax2, float* acc_o,
+                                      float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream);
+VOMNI_API int vomni_cm_attention_local_strided(const void* q, const void* k, const void* v, void* out, float* lse, int b,
+                                               int s, int h, int d, long long q_stride, long long kv_stride,
+                                               float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
+                                               vomni_stream_t stream);
 
 /* Single-rank (num_workers == 1) const-max attention: prologue + one final pass.
  * Replaces ring_attention_const_max_fwd(num_workers=1) (ring_attention_const_max_fwd.py:1306-1327).
@@ -157,6 +178,9 @@ VOMNI_API int vomni_ring_check(vomni_ring* ring);
 VOMNI_API int vomni_ring_attention(vomni_ring* ring, const void* q, const void* k, const void* v, void* out, float* lse,
                                    int b, int s_loc, int h, int d, float softmax_scale, int flags,
                                    vomni_stream_t stream);
+VOMNI_API int vomni_ring_attention_strided(vomni_ring* ring, const void* q, const void* k, const void* v, void* out,
+                                           float* lse, int b, int s_loc, int h, int d, long long q_stride,
+                                           long long kv_stride, float softmax_scale, int flags, vomni_stream_t stream);
 /* Pass plan (host-only, no GPU): pass 0 is the local block; pass i >= 1 covers gather slots
  * [first[i], first[i] + count[i]) with counts 1, 2, 4, ...; slot j holds ring step j + 1.
  * Returns the number of passes, or a negative status. */

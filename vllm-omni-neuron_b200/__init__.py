@@ -14,6 +14,7 @@ Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``
 from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .build import build
+from .leaf import wan_self_attention_fp8
 from .qkv import quantize_qkv_weight, repack_mx_contiguous, row_mx_qkv_proj
 from .ring import destroy_rings
 
@@ -27,4 +28,5 @@ __all__ = [
     "ring_attention_const_max_fwd",
     "row_mx_qkv_proj",
     "wan_cp_self_attention",
+    "wan_self_attention_fp8",
 ]

@@ -22,6 +22,7 @@ SIGNATURES = {
     "vomni_abi_version": (c_int, []),
     "vomni_strerror": (c_char_p, [c_int]),
     "vomni_device_status": (c_int, [ctypes.POINTER(c_int), c_int]),
+    "vomni_selftest_bounded_wait": (c_int, [ctypes.c_uint, ctypes.POINTER(c_int), P]),
     "vomni_cm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "vomni_cm_prologue": (c_int, [P, P, c_int, c_int, c_int, c_int, P, P, P]),
     "vomni_cm_attend": (
@@ -49,6 +50,19 @@ SIGNATURES = {
     ),
     "vomni_ring_phase_plan": (c_int, [c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_int), c_int]),
     "vomni_ring_source_rank": (c_int, [c_int, c_int, c_int]),
+    "vomni_cm_prologue_strided": (c_int, [P, P, c_int, c_int, c_int, c_int, ctypes.c_longlong, ctypes.c_longlong, P, P, P]),
+    "vomni_cm_attend_strided": (
+        c_int,
+        [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, ctypes.c_longlong, ctypes.c_longlong, c_float, P, P, P, P, c_int, P, P, P],
+    ),
+    "vomni_cm_attention_local_strided": (
+        c_int,
+        [P, P, P, P, P, c_int, c_int, c_int, c_int, ctypes.c_longlong, ctypes.c_longlong, c_float, c_int, P, c_size_t, P],
+    ),
+    "vomni_ring_attention_strided": (
+        c_int,
+        [P, P, P, P, P, P, c_int, c_int, c_int, c_int, ctypes.c_longlong, ctypes.c_longlong, c_float, c_int, P],
+    ),
     "vomni_cm_attention_local_noalloc": (
         c_int,
         [P, P, P, P, P, c_int, c_int, c_int, c_int, c_float, c_int, P],

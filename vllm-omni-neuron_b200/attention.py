@@ -42,6 +42,23 @@ def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     return b, s, h, d
 
 
+def token_major(t: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """(tensor, token stride in elements) for a token-major ``[b, s, h, d]`` view.
+
+    Views whose heads are dense inside a token row (for example the Q/K/V column slices of a fused
+    ``[b, s, 3*h*d]`` projection, ``tensor_split`` in row_mx_modules.py:390) are passed through with
+    their row stride; anything else is made contiguous."""
+    b, s, h, d = t.shape
+    st = t.stride()
+    ok = (
+        st[3] == 1 and st[2] == d and st[1] >= h * d and st[1] % 8 == 0
+        and (b == 1 or st[0] == s * st[1]) and t.data_ptr() % 16 == 0
+    )
+    if ok:
+        return t, st[1]
+    return t.contiguous(), h * d
+
+
 def _stream_ptr(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
@@ -61,7 +78,12 @@ def attention_local(
     layout). Returns ``o`` or ``(o, lse)``.
     """
     b, s, h, d = _check_qkv(q, k, v)
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    q, q_stride = token_major(q)
+    k, k_stride = token_major(k)
+    v, v_stride = token_major(v)
+    if k_stride != v_stride:  # K and V share one stride argument
+        k, v = k.contiguous(), v.contiguous()
+        k_stride = h * d
     scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
     lib = _lib.load()
     flags = 0
@@ -78,11 +100,11 @@ def attention_local(
         lse = torch.zeros((b, h, 128, -(-s // 128)), dtype=torch.float32, device=q.device)
     ws_bytes = lib.vomni_cm_workspace_bytes(b, s, h, d)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-    rc = lib.vomni_cm_attention_local(
+    rc = lib.vomni_cm_attention_local_strided(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if lse is not None else None,
-        b, s, h, d, scale, flags, ws.data_ptr(), ws_bytes, _stream_ptr(q.device),
+        b, s, h, d, q_stride, k_stride, scale, flags, ws.data_ptr(), ws_bytes, _stream_ptr(q.device),
     )
-    _lib.check(rc, "vomni_cm_attention_local")
+    _lib.check(rc, "vomni_cm_attention_local_strided")
     return (out, lse) if training else out
 
 

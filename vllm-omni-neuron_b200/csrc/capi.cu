@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <mutex>
 
+#include "common.cuh"
 #include "host_util.h"
 
 // One status word per device that loads the library; bounded device waits write their error
@@ -84,13 +85,14 @@ static int get_encoder() {
 }
 
 int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
-                      uint32_t box1) {
+                      uint32_t box1, uint64_t row_pitch_elems) {
   int rc = get_encoder();
   if (rc) return rc;
   if (reinterpret_cast<uintptr_t>(base) & 15) return VOMNI_EALIGN;
-  if ((dim0 * 2) % 16) return VOMNI_EALIGN;
+  if (row_pitch_elems == 0) row_pitch_elems = dim0;
+  if (row_pitch_elems < dim0 || (row_pitch_elems * 2) % 16) return VOMNI_EALIGN;
   cuuint64_t dims[3] = {dim0, dim1, dim2};
-  cuuint64_t strides[2] = {dim0 * 2, dim0 * dim1 * 2};
+  cuuint64_t strides[2] = {row_pitch_elems * 2, row_pitch_elems * dim1 * 2};
   cuuint32_t box[3] = {box0, box1, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
@@ -144,5 +146,40 @@ extern "C" int vomni_device_status(int* code, int clear) {
   VOMNI_CUDA_TRY(cudaDeviceSynchronize());
   VOMNI_CUDA_TRY(cudaMemcpy(code, p, sizeof(int), cudaMemcpyDeviceToHost));
   if (clear) VOMNI_CUDA_TRY(cudaMemset(p, 0, sizeof(int)));
+  return VOMNI_OK;
+}
+
+// ---------------------------------------------------------------- bounded-wait self-test
+// A CTA waits on an mbarrier that nothing ever arrives on, with a short budget. The bounded wait
+// must give up, record VOMNI_DEV_TIMEOUT_BASE + 0x7F in the status word and let the kernel end,
+// leaving the context usable. This exercises the failure path of every kernel's waits without
+// faulting, trapping or hanging the GPU.
+__global__ void selftest_wait_kernel(uint64_t budget_ns, int* status, int* result) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    vomni::mbar_init(&bar, 1);
+    abort_flag = 0;
+    vomni::fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = vomni::mbar_wait(&bar, 0, &abort_flag, status, VOMNI_DEV_TIMEOUT_BASE + 0x7F, budget_ns);
+  __syncthreads();
+  if (threadIdx.x == 0) *result = ok ? 1 : 0;
+}
+
+extern "C" int vomni_selftest_bounded_wait(unsigned budget_us, int* result_host, vomni_stream_t stream) {
+  if (!result_host || budget_us == 0 || budget_us > 2000000u) return VOMNI_EINVAL;
+  int* st = vomni::device_status_ptr();
+  if (!st) return VOMNI_ECUDA;
+  int* d = nullptr;
+  VOMNI_CUDA_TRY(cudaMalloc(&d, sizeof(int)));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  selftest_wait_kernel<<<1, 64, 0, s>>>(static_cast<uint64_t>(budget_us) * 1000ull, st, d);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaMemcpyAsync(result_host, d, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(d);
+  VOMNI_CUDA_TRY(e);
   return VOMNI_OK;
 }

@@ -357,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // per-head max of ||k||^2 folded through shared memory into kmax2 (atomicMax on the float bits,
 // valid because sums of squares are non-negative).
 __global__ void cm_norms_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, int b, int s,
-                                int h, float* __restrict__ qn2, unsigned int* __restrict__ kmax2_bits) {
+                                int h, long long q_stride, long long k_stride, float* __restrict__ qn2,
+                                unsigned int* __restrict__ kmax2_bits) {
   extern __shared__ unsigned int smax[];  // [b*h]
   const int bhn = b * h;
   for (int i = threadIdx.x; i < bhn; i += blockDim.x) smax[i] = 0u;
@@ -368,8 +369,9 @@ __global__ void cm_norms_kernel(const __nv_bfloat16* __restrict__ q, const __nv_
   const unsigned hmask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
   const int halves = (gridDim.x * blockDim.x) >> 4;
   for (long long r = half; r < rows; r += halves) {
-    const uint4 qv = reinterpret_cast<const uint4*>(q + r * kD)[sub];
-    const uint4 kv = reinterpret_cast<const uint4*>(k + r * kD)[sub];
+    const long long tok_r = r / h, hd = (r % h) * kD;  // token-major rows, tokens `stride` apart
+    const uint4 qv = reinterpret_cast<const uint4*>(q + tok_r * q_stride + hd)[sub];
+    const uint4 kv = reinterpret_cast<const uint4*>(k + tok_r * k_stride + hd)[sub];
     float sq = 0.f, sk = 0.f;
     const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qv);
     const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
@@ -412,12 +414,16 @@ extern "C" size_t vomni_cm_workspace_bytes(int b, int s, int h, int d) {
   return align_up(qn, 256) + align_up(km, 256);
 }
 
-extern "C" int vomni_cm_prologue(const void* q, const void* k, int b, int s, int h, int d, float* qn2, float* kmax2,
-                                 vomni_stream_t stream) {
+extern "C" int vomni_cm_prologue_strided(const void* q, const void* k, int b, int s, int h, int d, long long q_stride,
+                                         long long k_stride, float* qn2, float* kmax2, vomni_stream_t stream) {
   if (!q || !k || !qn2 || !kmax2) return VOMNI_EINVAL;
   if (d != cm::kD || b <= 0 || s <= 0 || h <= 0) return VOMNI_EBADSHAPE;
   if (b * h > 8192) return VOMNI_EBADSHAPE;
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15) return VOMNI_EALIGN;
+  if (q_stride == 0) q_stride = static_cast<long long>(h) * d;
+  if (k_stride == 0) k_stride = static_cast<long long>(h) * d;
+  if (q_stride < static_cast<long long>(h) * d || k_stride < static_cast<long long>(h) * d) return VOMNI_EBADSHAPE;
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15) || ((q_stride | k_stride) & 7))
+    return VOMNI_EALIGN;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   VOMNI_CUDA_TRY(cudaMemsetAsync(kmax2, 0, sizeof(float) * b * h, st));
   const long long rows = static_cast<long long>(b) * s * h;
@@ -426,15 +432,21 @@ extern "C" int vomni_cm_prologue(const void* q, const void* k, int b, int s, int
   const int max_blocks = num_sms() * 8;
   if (blocks > max_blocks) blocks = max_blocks;
   cm::cm_norms_kernel<<<static_cast<int>(blocks), threads, sizeof(unsigned) * b * h, st>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), b, s, h, qn2,
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), b, s, h, q_stride, k_stride, qn2,
       reinterpret_cast<unsigned int*>(kmax2));
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }
 
-extern "C" int vomni_cm_attend(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start,
-                               int n_keys, int h, int d, float softmax_scale, const float* qn2, const float* kmax2,
-                               float* acc_o, float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream) {
+extern "C" int vomni_cm_prologue(const void* q, const void* k, int b, int s, int h, int d, float* qn2, float* kmax2,
+                                 vomni_stream_t stream) {
+  return vomni_cm_prologue_strided(q, k, b, s, h, d, 0, 0, qn2, kmax2, stream);
+}
+
+extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void* v, int b, int s_q, int s_kv,
+                                       int k_start, int n_keys, int h, int d, long long q_stride, long long kv_stride,
+                                       float softmax_scale, const float* qn2, const float* kmax2, float* acc_o,
+                                       float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream) {
   if (!q || !k || !v || !qn2 || !kmax2) return VOMNI_EINVAL;
   if (d != cm::kD || b <= 0 || s_q <= 0 || h <= 0 || n_keys <= 0 || k_start < 0 || k_start + n_keys > s_kv)
     return VOMNI_EBADSHAPE;
@@ -451,12 +463,15 @@ extern "C" int vomni_cm_attend(const void* q, const void* k, const void* v, int 
   if (rc) return rc;
 
   const uint64_t row_elems = static_cast<uint64_t>(h) * cm::kD;
+  if (q_stride == 0) q_stride = static_cast<long long>(row_elems);
+  if (kv_stride == 0) kv_stride = static_cast<long long>(row_elems);
+  if (q_stride < static_cast<long long>(row_elems) || kv_stride < static_cast<long long>(row_elems)) return VOMNI_EBADSHAPE;
   CUtensorMap tq, tk, tv;
-  rc = make_tmap_3d_bf16(&tq, q, row_elems, s_q, b, 64, 128);
+  rc = make_tmap_3d_bf16(&tq, q, row_elems, s_q, b, 64, 128, static_cast<uint64_t>(q_stride));
   if (rc) return rc;
-  rc = make_tmap_3d_bf16(&tk, k, row_elems, s_kv, b, 64, 128);
+  rc = make_tmap_3d_bf16(&tk, k, row_elems, s_kv, b, 64, 128, static_cast<uint64_t>(kv_stride));
   if (rc) return rc;
-  rc = make_tmap_3d_bf16(&tv, v, row_elems, s_kv, b, 64, 128);
+  rc = make_tmap_3d_bf16(&tv, v, row_elems, s_kv, b, 64, 128, static_cast<uint64_t>(kv_stride));
   if (rc) return rc;
 
   cm::Params p;
@@ -496,9 +511,17 @@ extern "C" int vomni_cm_attend(const void* q, const void* k, const void* v, int 
   return VOMNI_OK;
 }
 
-extern "C" int vomni_cm_attention_local(const void* q, const void* k, const void* v, void* out, float* lse, int b, int s,
-                                        int h, int d, float softmax_scale, int flags, void* workspace,
-                                        size_t workspace_bytes, vomni_stream_t stream) {
+extern "C" int vomni_cm_attend(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start,
+                               int n_keys, int h, int d, float softmax_scale, const float* qn2, const float* kmax2,
+                               float* acc_o, float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream) {
+  return vomni_cm_attend_strided(q, k, v, b, s_q, s_kv, k_start, n_keys, h, d, 0, 0, softmax_scale, qn2, kmax2, acc_o,
+                                 acc_l, flags, out, lse, stream);
+}
+
+extern "C" int vomni_cm_attention_local_strided(const void* q, const void* k, const void* v, void* out, float* lse, int b,
+                                                int s, int h, int d, long long q_stride, long long kv_stride,
+                                                float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
+                                                vomni_stream_t stream) {
   if (!workspace) return VOMNI_EINVAL;
   if (flags & ~(VOMNI_CM_OUT_DMAJOR | VOMNI_CM_LSE)) return VOMNI_EINVAL;
   const size_t need = vomni_cm_workspace_bytes(b, s, h, d);
@@ -507,10 +530,17 @@ extern "C" int vomni_cm_attention_local(const void* q, const void* k, const void
   float* qn2 = static_cast<float*>(workspace);
   float* kmax2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
                                           align_up(static_cast<size_t>(b) * h * s * sizeof(float), 256));
-  int rc = vomni_cm_prologue(q, k, b, s, h, d, qn2, kmax2, stream);
+  int rc = vomni_cm_prologue_strided(q, k, b, s, h, d, q_stride, kv_stride, qn2, kmax2, stream);
   if (rc) return rc;
-  return vomni_cm_attend(q, k, v, b, s, s, 0, s, h, d, softmax_scale, qn2, kmax2, nullptr, nullptr,
-                         flags | VOMNI_CM_FINAL, out, lse, stream);
+  return vomni_cm_attend_strided(q, k, v, b, s, s, 0, s, h, d, q_stride, kv_stride, softmax_scale, qn2, kmax2, nullptr,
+                                 nullptr, flags | VOMNI_CM_FINAL, out, lse, stream);
+}
+
+extern "C" int vomni_cm_attention_local(const void* q, const void* k, const void* v, void* out, float* lse, int b, int s,
+                                        int h, int d, float softmax_scale, int flags, void* workspace,
+                                        size_t workspace_bytes, vomni_stream_t stream) {
+  return vomni_cm_attention_local_strided(q, k, v, out, lse, b, s, h, d, 0, 0, softmax_scale, flags, workspace,
+                                          workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------- allocation-free variant

@@ -67,13 +67,14 @@ VOMNI_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint
 
 // Wait until the phase with parity `parity` of `bar` has completed. Returns false (and raises
 // `*abort`) when the budget runs out or another thread of the CTA already aborted.
-VOMNI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status, int code) {
+VOMNI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status, int code,
+                         uint64_t budget_ns = kWaitBudgetNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 200000u)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitBudgetNs) {
+    if (globaltimer() - t0 > budget_ns) {
       *abort = 1;
       if (status) atomicCAS(status, 0, code);
       return false;

@@ -287,9 +287,10 @@ extern "C" int vomni_ring_check(vomni_ring* R) {
   return VOMNI_OK;
 }
 
-extern "C" int vomni_ring_attention(vomni_ring* R, const void* q, const void* k, const void* v, void* out, float* lse,
-                                    int b, int s_loc, int h, int d, float softmax_scale, int flags,
-                                    vomni_stream_t stream) {
+extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const void* k, const void* v, void* out,
+                                            float* lse, int b, int s_loc, int h, int d, long long q_stride,
+                                            long long kv_stride, float softmax_scale, int flags,
+                                            vomni_stream_t stream) {
   if (!R || !q || !k || !v || !out) return VOMNI_EINVAL;
   if (R->broken) return VOMNI_ESTATE;
   if (flags & ~(VOMNI_CM_OUT_DMAJOR | VOMNI_CM_LSE)) return VOMNI_EINVAL;
@@ -302,13 +303,18 @@ extern "C" int vomni_ring_attention(vomni_ring* R, const void* q, const void* k,
   if (!n) return VOMNI_ENCCL;
   const int N = R->world;
   const size_t blk = static_cast<size_t>(s_loc) * h * d * 2;  // one batch row-block of K or V
+  const long long dense = static_cast<long long>(h) * d;
+  if (q_stride == 0) q_stride = dense;
+  if (kv_stride == 0) kv_stride = dense;
+  if (q_stride < dense || kv_stride < dense) return VOMNI_EBADSHAPE;
+  if ((q_stride | kv_stride) & 7) return VOMNI_EALIGN;
   int rc;
 
   if (N == 1) {
-    rc = vomni_cm_prologue(q, k, b, s_loc, h, d, R->qn2, R->kmax2, stream);
+    rc = vomni_cm_prologue_strided(q, k, b, s_loc, h, d, q_stride, kv_stride, R->qn2, R->kmax2, stream);
     if (rc) return rc;
-    return vomni_cm_attend(q, k, v, b, s_loc, s_loc, 0, s_loc, h, d, softmax_scale, R->qn2, R->kmax2, nullptr, nullptr,
-                           flags | VOMNI_CM_FINAL, out, lse, stream);
+    return vomni_cm_attend_strided(q, k, v, b, s_loc, s_loc, 0, s_loc, h, d, q_stride, kv_stride, softmax_scale, R->qn2,
+                                   R->kmax2, nullptr, nullptr, flags | VOMNI_CM_FINAL, out, lse, stream);
   }
 
   const int parity = static_cast<int>(R->calls & 1);
@@ -317,14 +323,17 @@ extern "C" int vomni_ring_attention(vomni_ring* R, const void* q, const void* k,
   //    buffer keeps an s_max stride per batch so peers address it with the creation-time geometry).
   uint8_t* my_send = static_cast<uint8_t*>(R->send) + static_cast<size_t>(parity) * 2 * R->block_bytes;
   const size_t bstride = static_cast<size_t>(R->s_max) * h * d * 2;
+  const size_t src_bstride = static_cast<size_t>(s_loc) * kv_stride * 2;  // a strided view's batch stride
+  const size_t row_bytes = static_cast<size_t>(dense) * 2;
   for (int bi = 0; bi < b; ++bi) {
-    VOMNI_CUDA_TRY(cudaMemcpyAsync(my_send + bi * bstride, static_cast<const uint8_t*>(k) + bi * blk, blk,
-                                   cudaMemcpyDeviceToDevice, st));
-    VOMNI_CUDA_TRY(cudaMemcpyAsync(my_send + R->block_bytes + bi * bstride, static_cast<const uint8_t*>(v) + bi * blk,
-                                   blk, cudaMemcpyDeviceToDevice, st));
+    VOMNI_CUDA_TRY(cudaMemcpy2DAsync(my_send + bi * bstride, row_bytes, static_cast<const uint8_t*>(k) + bi * src_bstride,
+                                     static_cast<size_t>(kv_stride) * 2, row_bytes, s_loc, cudaMemcpyDeviceToDevice, st));
+    VOMNI_CUDA_TRY(cudaMemcpy2DAsync(my_send + R->block_bytes + bi * bstride, row_bytes,
+                                     static_cast<const uint8_t*>(v) + bi * src_bstride, static_cast<size_t>(kv_stride) * 2,
+                                     row_bytes, s_loc, cudaMemcpyDeviceToDevice, st));
   }
   // 2. local norms, 3. global key max (also the "peers' blocks are published" point)
-  rc = vomni_cm_prologue(q, k, b, s_loc, h, d, R->qn2, R->kmax2, stream);
+  rc = vomni_cm_prologue_strided(q, k, b, s_loc, h, d, q_stride, kv_stride, R->qn2, R->kmax2, stream);
   if (rc) return rc;
   if (n->AllReduce(R->kmax2, R->kmax2, static_cast<size_t>(b) * h, ncclFloat32, ncclMax, R->comm, st) != ncclSuccess) {
     R->broken = true;
@@ -349,17 +358,23 @@ extern "C" int vomni_ring_attention(vomni_ring* R, const void* q, const void* k,
   int first[64], count[64];
   const int np = vomni_ring_phase_plan(N, first, count, 64);
   if (np < 2) return VOMNI_EINVAL;
-  rc = vomni_cm_attend(q, k, v, b, s_loc, s_loc, 0, s_loc, h, d, softmax_scale, R->qn2, R->kmax2, R->acc_o, R->acc_l,
-                       0, nullptr, nullptr, stream);
+  rc = vomni_cm_attend_strided(q, k, v, b, s_loc, s_loc, 0, s_loc, h, d, q_stride, kv_stride, softmax_scale, R->qn2,
+                               R->kmax2, R->acc_o, R->acc_l, 0, nullptr, nullptr, stream);
   if (rc) return rc;
   const int s_kv = (N - 1) * s_loc;
   for (int p = 1; p < np; ++p) {
     const int last_step = first[p] + count[p];  // ring step of the last block in this pass
     VOMNI_CUDA_TRY(cudaStreamWaitEvent(st, R->ev_block[last_step], 0));
     const int fl = VOMNI_CM_ACC_IN | (p == np - 1 ? (VOMNI_CM_FINAL | flags) : 0);
-    rc = vomni_cm_attend(q, R->gather_k, R->gather_v, b, s_loc, s_kv, first[p] * s_loc, count[p] * s_loc, h, d,
-                         softmax_scale, R->qn2, R->kmax2, R->acc_o, R->acc_l, fl, out, lse, stream);
+    rc = vomni_cm_attend_strided(q, R->gather_k, R->gather_v, b, s_loc, s_kv, first[p] * s_loc, count[p] * s_loc, h, d,
+                                 q_stride, 0, softmax_scale, R->qn2, R->kmax2, R->acc_o, R->acc_l, fl, out, lse, stream);
     if (rc) return rc;
   }
   return VOMNI_OK;
+}
+
+extern "C" int vomni_ring_attention(vomni_ring* R, const void* q, const void* k, const void* v, void* out, float* lse,
+                                    int b, int s_loc, int h, int d, float softmax_scale, int flags,
+                                    vomni_stream_t stream) {
+  return vomni_ring_attention_strided(R, q, k, v, out, lse, b, s_loc, h, d, 0, 0, softmax_scale, flags, stream);
 }

@@ -1,0 +1,68 @@
+"""The FP8 self-attention leaf: fused ROW FP8 QKV projection -> const-max (ring) attention.
+
+Mirrors ``WanSelfAttentionFP8.forward`` (vllm_omni_neuron/diffusion/quantization/row_mx_modules.py:
+340-404) up to the attention output (the o-projection that follows, :404, is outside this path):
+
+1. rotate-half cos/sin caches from Wan's interleaved RoPE tables (:356-366, ``_rope_rotate_half_caches``);
+2. ``row_mx_qkv_proj`` with the across-heads RMS qk-norm (gammas de-interleaved at load time) and the
+   fused rotate-half RoPE (:367-389);
+3. ``tensor_split`` into Q/K/V token-major views (:390-393) — passed to the attention with their row
+   stride, no copy;
+4. ``wan_cp_self_attention`` (:395-403), d-major ``[B, N, D, S_loc]`` result.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .attention import wan_cp_self_attention
+from .qkv import row_mx_qkv_proj
+from .rope import rope_rotate_half_caches
+
+
+def wan_self_attention_fp8(
+    hidden_states,
+    qkv_proj_weight: torch.Tensor,
+    qkv_proj_w_scale: torch.Tensor,
+    qkv_proj_bias: torch.Tensor | None,
+    norm_q_weight: torch.Tensor | None,
+    norm_k_weight: torch.Tensor | None,
+    rotary_emb=None,
+    *,
+    num_heads: int,
+    head_dim: int = 128,
+    eps: float = 1e-6,
+    scale: float | None = None,
+    cp_size: int = 1,
+    cp_group=None,
+    cp_replica_groups=None,
+):
+    """``hidden_states``: the packed ``[B, S_loc, H + 4]`` FP8 rows from ``adaln_modulate(quant="row")``
+    or its ``(codes, scales)`` split form. Weights are the de-interleaved fused Q|K|V ``[I, H]`` FP8
+    codes with per-channel scales (``quantize_qkv_weight`` of ``deinterleave_qk_columns(W)``).
+    ``rotary_emb``: Wan's interleaved ``(freqs_cos, freqs_sin)`` for this rank's tokens."""
+    if isinstance(hidden_states, (tuple, list)):
+        b, s = hidden_states[0].shape[0], hidden_states[0].shape[1]
+    else:
+        b, s = hidden_states.shape[0], hidden_states.shape[1]
+    cos_cache = sin_cache = None
+    if rotary_emb is not None:
+        cos_rh, sin_rh = rope_rotate_half_caches(*rotary_emb)
+        cos_cache = cos_rh.reshape(1, s, head_dim).expand(b, s, head_dim).contiguous()
+        sin_cache = sin_rh.reshape(1, s, head_dim).expand(b, s, head_dim).contiguous()
+    qkv = row_mx_qkv_proj(
+        hidden_states, qkv_proj_weight, qkv_proj_w_scale, qkv_proj_bias,
+        num_heads=num_heads, head_dim=head_dim, num_kv_heads=num_heads,
+        fused_rope=rotary_emb is not None, cos_cache=cos_cache, sin_cache=sin_cache,
+        qk_norm_pre_rope=True, qk_norm_pre_rope_q_gamma=norm_q_weight, qk_norm_pre_rope_k_gamma=norm_k_weight,
+        norm_eps=eps,
+    )
+    query, key, value = torch.tensor_split(qkv, 3, dim=-1)
+    query = query.unflatten(2, (num_heads, head_dim))
+    key = key.unflatten(2, (num_heads, head_dim))
+    value = value.unflatten(2, (num_heads, head_dim))
+    return wan_cp_self_attention(
+        query, key, value, scale if scale else 1.0 / math.sqrt(head_dim), cp_size, cp_group, cp_replica_groups
+    )

@@ -109,7 +109,14 @@ def ring_attention(
     # kv_prefetch_depth is clamped as the reference does (:1078); the copy engine pulls every block
     # as soon as the key max is reduced, and the pass plan gates compute on arrival.
     _ = min(max(int(kv_prefetch_depth), 1), max(num_workers - 1, 1))
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    from .attention import token_major
+
+    q, q_stride = token_major(q)
+    k, k_stride = token_major(k)
+    v, v_stride = token_major(v)
+    if k_stride != v_stride:
+        k, v = k.contiguous(), v.contiguous()
+        k_stride = h * d
     ring = get_ring(group, b, s, h, d)
     scale = float(softmax_scale) if softmax_scale else 1.0 / math.sqrt(d)
     flags = 0
@@ -124,12 +131,12 @@ def ring_attention(
     if training:
         flags |= _lib.CM_LSE
         lse = torch.zeros((b, h, 128, -(-s // 128)), dtype=torch.float32, device=q.device)
-    rc = _lib.load().vomni_ring_attention(
+    rc = _lib.load().vomni_ring_attention_strided(
         ring.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-        lse.data_ptr() if lse is not None else None, b, s, h, d, scale, flags,
+        lse.data_ptr() if lse is not None else None, b, s, h, d, q_stride, k_stride, scale, flags,
         torch.cuda.current_stream(q.device).cuda_stream,
     )
-    _lib.check(rc, "vomni_ring_attention")
+    _lib.check(rc, "vomni_ring_attention_strided")
     return (out, lse) if training else out
 
 
