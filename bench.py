@@ -452,7 +452,7 @@ def run_c3(args, emit):
     codes = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=dev)
     scales = torch.empty(T, dtype=torch.float32, device=dev)
     y = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
-    sumsq = torch.empty(T, 2 * H // 256, dtype=torch.float32, device=dev)
+    sumsq = torch.empty(T, 2 * H // HEAD_DIM, dtype=torch.float32, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2: flushed between launches
 
     def adaln():
@@ -462,6 +462,21 @@ def run_c3(args, emit):
     def gemm():
         lib.check(L.vomni_qkv_fp8_gemm(codes.data_ptr(), scales.data_ptr(), wq.data_ptr(), chan.data_ptr(), bias.data_ptr(),
                                        T, H, I, H, H, y.data_ptr(), sumsq.data_ptr(), st), "gemm")
+
+    # MX-32 variant (UE8M0 per 32 contraction values on activations and weights)
+    wmx, _, wmx_sf = pkg.quantize_qkv_weight_mx32(w)
+    mx_codes = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=dev)
+    mx_scales = torch.empty(T, H // 32, dtype=torch.uint8, device=dev)
+    mx_packed = torch.empty(L.vomni_mx_packed_scales_bytes(T, H), dtype=torch.uint8, device=dev)
+
+    def adaln_mx():
+        lib.check(L.vomni_adaln_modulate(hidden.data_ptr(), None, mul.data_ptr(), add.data_ptr(), None, T, H, T, 1e-6, 0, 2, 1,
+                                         0, mx_codes.data_ptr(), mx_scales.data_ptr(), None, st), "adaln mx32")
+        lib.check(L.vomni_mx_pack_scales(mx_scales.data_ptr(), T, H, mx_packed.data_ptr(), st), "pack")
+
+    def gemm_mx():
+        lib.check(L.vomni_qkv_mx32_gemm(mx_codes.data_ptr(), mx_packed.data_ptr(), wmx.data_ptr(), wmx_sf.data_ptr(),
+                                        bias.data_ptr(), T, H, I, H, H, y.data_ptr(), sumsq.data_ptr(), st), "gemm mx32")
 
     def apply():
         lib.check(L.vomni_qk_norm_rope(y.data_ptr(), T, I, HEADS, HEADS, HEAD_DIM, sumsq.data_ptr(), 1e-6, gamma.data_ptr(),
@@ -479,7 +494,7 @@ def run_c3(args, emit):
             ts.append(a.elapsed_time(b))
         return statistics.median(ts)
 
-    for fn in (adaln, gemm, apply):
+    for fn in (adaln, gemm, apply, adaln_mx, gemm_mx):
         for _ in range(args.warmup):
             fn()
     torch.cuda.synchronize()
@@ -487,14 +502,16 @@ def run_c3(args, emit):
     sampler = ClockSampler(0)
     sampler.start()
     t_ad, t_gm, t_ap = timeit(adaln, n), timeit(gemm, n), timeit(apply, n)
+    t_admx, t_gmmx = timeit(adaln_mx, n), timeit(gemm_mx, n)
     clocks = sampler.stop()
     assert lib.device_status() == 0
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = peaks.get("hbm_gbs", 6650.0)
     bf16 = peaks.get("bf16_tflops", 1590.0)
     ad_bytes = 2 * T * H + T * H + 4 * T
-    ap_bytes = 2 * (2 * T * 2 * H) + T * (2 * H // 256) * 4 + 2 * T * HEAD_DIM * 4
+    ap_bytes = 2 * (2 * T * 2 * H) + T * (2 * H // HEAD_DIM) * 4 + 2 * T * HEAD_DIM * 4
     gm_flops = 2.0 * T * H * I
+    admx_bytes = 2 * T * H + T * H + 3 * (T * H // 32)  # bf16 in, codes out, scales out, re-tiled (read + write)
     res = {
         "metric": "C3 fused adaLN + FP8 row quant + FP8 QKV projection (ms per call, per kernel)",
         "value": round(t_ad + t_gm + t_ap, 4), "unit": "ms", "higher_is_better": False, "n_gpus": 1,
@@ -507,9 +524,15 @@ def run_c3(args, emit):
                              "frac_of_measured_bf16_burst_x2": round(gm_flops / t_gm / 1e9 / (2 * bf16), 4)},
             "qk_norm_rope": {"ms": round(t_ap, 4), "bytes": ap_bytes, "GB/s": round(ap_bytes / t_ap / 1e6, 1),
                              "frac_of_measured_hbm": round(ap_bytes / t_ap / 1e6 / hbm, 4)},
+            "adaln_mx32quant_and_scale_pack": {"ms": round(t_admx, 4), "bytes": admx_bytes,
+                                               "GB/s": round(admx_bytes / t_admx / 1e6, 1),
+                                               "frac_of_measured_hbm": round(admx_bytes / t_admx / 1e6 / hbm, 4)},
+            "qkv_mx32_gemm": {"ms": round(t_gmmx, 4), "flops": gm_flops, "TFLOP/s": round(gm_flops / t_gmmx / 1e9, 1),
+                              "frac_of_measured_bf16_burst_x2": round(gm_flops / t_gmmx / 1e9 / (2 * bf16), 4)},
         },
+        "mx32_path_ms": round(t_admx + t_gmmx + t_ap, 4),
         "clocks": clocks,
-        "gpu_launches": 3 * n,
+        "gpu_launches": 6 * n,
     }
     emit(res)
 

@@ -137,9 +137,9 @@ VOMNI_API int vomni_adaln_modulate(const void* hidden, const void* residual, con
  *
  * vomni_qkv_fp8_gemm: y[t, i] = bf16(sum_h x[t, h] w[i, h] * row_scale[t] * chan_scale[i] + bias[i])
  * (_dequant_row_mx, qkv_cte.py:3996-4021). x_codes: e4m3fn [t, h]; w_codes: e4m3fn [i, h] (K-major);
- * bias bf16 [i] or NULL; y bf16 [t, i]. If sumsq is non-NULL it receives, per row, the partial sums
- * of squares of the stored bf16 y over each 256-column tile of the Q and K segments
- * ([t, (q_dim + kv_dim) / 256] fp32), the input of the across-heads RMS (qkv_cte.py:3870-3898).
+ * bias bf16 [i] or NULL; y bf16 [t, i]. If sumsq is non-NULL it receives, per row, the sums of
+ * squares of the stored bf16 y over each 128-column head of the Q and K segments
+ * ([t, (q_dim + kv_dim) / 128] fp32), the input of the across-heads RMS (qkv_cte.py:3870-3898).
  * h % 128 == 0, i % 256 == 0, q_dim % 256 == 0, kv_dim % 256 == 0. */
 VOMNI_API int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, const void* w_codes,
                                  const float* chan_scale, const void* bias, int t, int h, int i, int q_dim, int kv_dim,
@@ -150,6 +150,17 @@ VOMNI_API int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, co
 VOMNI_API int vomni_qk_norm_rope(void* y, int t, int i, int q_heads, int kv_heads, int head_dim, const float* sumsq,
                                  float eps, const void* gamma_q, const void* gamma_k, const float* cos, const float* sin,
                                  vomni_stream_t stream);
+/* MX-32 mode (block-scaled tcgen05 GEMM, kind::mxf8f6f4.block_scale; the MX-32 format of
+ * _mx_dequant, kernels/nkilib/experimental/norm/adaln_quant_torch.py:151-175):
+ * y[t, i] = bf16(sum over 32-blocks of (x codes * 2^(sx-127)) . (w codes * 2^(sw-127)) + bias[i]),
+ * same sumsq partials as vomni_qkv_fp8_gemm. Scale factors (UE8M0 bytes, [rows, h/32] row-major as
+ * vomni_adaln_modulate quant 2 writes them) must first be re-tiled with vomni_mx_pack_scales into
+ * vomni_mx_packed_scales_bytes(rows, h) bytes (weights: once, at load time). */
+VOMNI_API size_t vomni_mx_packed_scales_bytes(int rows, int k);
+VOMNI_API int vomni_mx_pack_scales(const void* sf, int rows, int k, void* out, vomni_stream_t stream);
+VOMNI_API int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed, const void* w_codes,
+                                  const void* w_sf_packed, const void* bias, int t, int h, int i, int q_dim, int kv_dim,
+                                  void* y, float* sumsq, vomni_stream_t stream);
 /* [t, h + 4] packed rows (adaln ROW output) -> codes [t, h] + scales [t]. */
 VOMNI_API int vomni_qkv_unpack_rows(const void* packed, int t, int h, void* codes, float* scales, vomni_stream_t stream);
 

@@ -132,3 +132,65 @@ def test_errors(pkg, dev):
         pkg.row_mx_qkv_proj(packed, wq, chan, bias, num_heads=2, head_dim=128, num_kv_heads=2)
     with pytest.raises(NotImplementedError):
         pkg.row_mx_qkv_proj(packed, wq, chan, bias, num_heads=2, head_dim=128, num_kv_heads=2, replica_groups=((0, 1),))
+
+
+def _mx_pack_ref(sc: np.ndarray) -> np.ndarray:
+    """Scale-atom tiling of [rows, k/32] UE8M0 scales: tiles [k/128][ceil(rows/128)][512], byte
+    m0*16 + m1*4 + j of a tile = row 32*m1 + m0, scale block j; rows past the end hold 127 (2^0)."""
+    rows, kb = sc.shape
+    rb = -(-rows // 128)
+    pad = np.full((rb * 128, kb), 127, np.uint8)
+    pad[:rows] = sc
+    t = pad.reshape(rb, 4, 32, kb // 4, 4)  # [rb, m1, m0, kb4, j]
+    return np.ascontiguousarray(t.transpose(3, 0, 2, 1, 4)).reshape(-1)
+
+
+@pytest.mark.parametrize("rows,k", [(300, 512), (128, 128), (1, 256)])
+def test_mx_scale_pack_layout(pkg, dev, rows, k):
+    g = torch.Generator().manual_seed(rows)
+    sc = torch.randint(100, 150, (rows, k // 32), generator=g, dtype=torch.uint8)
+    got = pkg.pack_mx_scales(sc.to(dev)).cpu().numpy()
+    assert np.array_equal(got, _mx_pack_ref(sc.numpy()))
+
+
+@pytest.mark.parametrize("T,H,heads", [(300, 512, 2), (129, 1024, 4), (1, 512, 2), (1000, 1024, 2)])
+def test_mx32_gemm_vs_oracle(pkg, dev, T, H, heads):
+    """Block-scaled tcgen05 MMA (UE8M0 per 32 contraction values on both operands) against the oracle
+    on the same dequantised operands."""
+    hidden, w, bias, I = _setup(T, H, heads, dev, seed=4)
+    # a few large outliers so the 32-blocks carry different scales
+    hidden[:, ::97] *= 40
+    xc, xs = pkg.adaln_modulate(hidden, None, None, eps=1e-6, norm_type="none", quant="mx32")
+    wc, ws, wsp = pkg.quantize_qkv_weight_mx32(w)
+    y = pkg.mx32_qkv_proj((xc, xs), wc, wsp, bias, num_heads=heads, head_dim=128, num_kv_heads=heads)
+    torch.cuda.synchronize()
+    deq = lambda c, s: (e4m3fn_from_bits(c.view(torch.uint8).cpu().numpy()).reshape(c.shape[0], -1, 32)
+                        * np.exp2(s.cpu().numpy().astype(np.float64) - 127)[..., None]).reshape(c.shape[0], -1)
+    xd, wd = deq(xc, xs), deq(wc, ws)  # [T, H], [I, H]
+    assert len(np.unique(xs.cpu().numpy())) > 1 and len(np.unique(ws.cpu().numpy())) > 1
+    # weight quant = the oracle's MX-32 quant of the bf16 weight
+    _, ws_ref, wd_ref = oq.mx32_weight_quant(w.to(torch.bfloat16).float().cpu().numpy())
+    assert np.array_equal(ws.cpu().numpy(), ws_ref.T) and np.array_equal(wd.astype(np.float32), wd_ref.T)
+    ref = oq.mx32_qkv_ref(xd, wd.T, bias.float().cpu().numpy())
+    got = y.float().cpu().numpy()
+    _cmp(got, ref, 0.99999, 1e-2 * max(1.0, np.abs(ref).max()), f"mx32 gemm {T}x{H}x{I}")
+    assert (np.abs(got - ref) <= np.abs(ref) * 2 ** -7 + 1e-3).mean() > 0.999
+
+
+def test_mx32_norm_rope_epilogue(pkg, dev):
+    T, H, heads = 257, 1024, 4
+    hidden, w, bias, I = _setup(T, H, heads, dev, seed=6)
+    rope = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.rope")
+    cos, sin = rope.wan_rotary_freqs(128, (1, 2, 2), 1024, (3, 20, 40), device=dev)
+    cos_rh, sin_rh = rope.rope_rotate_half_caches(cos[:, :T], sin[:, :T])
+    xc, xs = pkg.adaln_modulate(hidden, None, None, eps=1e-6, norm_type="layer_norm", quant="mx32")
+    wc, ws, wsp = pkg.quantize_qkv_weight_mx32(w)
+    y = pkg.mx32_qkv_proj((xc, xs), wc, wsp, bias, num_heads=heads, head_dim=128, num_kv_heads=heads, fused_rope=True,
+                          cos_cache=cos_rh, sin_cache=sin_rh, qk_norm_pre_rope=True)
+    torch.cuda.synchronize()
+    deq = lambda c, s: (e4m3fn_from_bits(c.view(torch.uint8).cpu().numpy()).reshape(c.shape[0], -1, 32)
+                        * np.exp2(s.cpu().numpy().astype(np.float64) - 127)[..., None]).reshape(c.shape[0], -1)
+    ref = oq.mx32_qkv_ref(deq(xc, xs), deq(wc, ws).T, bias.float().cpu().numpy(), num_heads=heads, head_dim=128,
+                          num_kv_heads=heads, cos=cos_rh.reshape(T, 128).cpu().numpy(),
+                          sin=sin_rh.reshape(T, 128).cpu().numpy(), eps=1e-6)
+    _cmp(y.float().cpu().numpy(), ref, 0.99999, 3e-2, "mx32 epilogue")

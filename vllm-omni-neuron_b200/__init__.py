@@ -15,7 +15,14 @@ from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .build import build
 from .leaf import wan_self_attention_fp8
-from .qkv import quantize_qkv_weight, repack_mx_contiguous, row_mx_qkv_proj
+from .qkv import (
+    mx32_qkv_proj,
+    pack_mx_scales,
+    quantize_qkv_weight,
+    quantize_qkv_weight_mx32,
+    repack_mx_contiguous,
+    row_mx_qkv_proj,
+)
 from .ring import destroy_rings
 
 __all__ = [
@@ -23,7 +30,10 @@ __all__ = [
     "attention_local",
     "build",
     "destroy_rings",
+    "mx32_qkv_proj",
+    "pack_mx_scales",
     "quantize_qkv_weight",
+    "quantize_qkv_weight_mx32",
     "repack_mx_contiguous",
     "ring_attention_const_max_fwd",
     "row_mx_qkv_proj",

@@ -144,6 +144,22 @@ VOMNI_DEV void mma_f8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem] with per-32-element UE8M0 block scales read from TMEM
+// (kind::mxf8f6f4.block_scale, e4m3 operands, fp32 accumulate). The instruction descriptor's
+// a_sf_id / b_sf_id select which byte of each 32-bit scale word this K=32 step uses.
+VOMNI_DEV void mma_mxf8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum,
+                           uint32_t sfa_tmem, uint32_t sfb_tmem) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// Shared memory -> TMEM copy of 32 rows x 128 bits, replicated into all four lane quadrants.
+VOMNI_DEV void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets lane (warp%4)*32 + t.
 VOMNI_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -195,6 +211,12 @@ VOMNI_DEV uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_b
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
+}
+// Instruction descriptor, kind::mxf8f6f4.block_scale: e4m3 A/B (K-major), UE8M0 scales (bit 23),
+// fp32 D, scale byte `sf_id` of each 32-bit scale word for both A (bits 29-30) and B (bits 4-5).
+__host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n, uint32_t sf_id) {
+  return ((sf_id & 3u) << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) |
+         (static_cast<uint32_t>(m >> 4) << 24) | ((sf_id & 3u) << 29);
 }
 // Instruction descriptor, kind::f8f6f4 with e4m3 A/B (both K-major) and fp32 D.
 __host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n) {

@@ -43,8 +43,8 @@ struct Params {
   const float* chan_scale;  // [I]
   const __nv_bfloat16* bias;  // [I] or null
   __nv_bfloat16* y;           // [T, I]
-  float* sumsq;               // [T, n_norm_tiles] or null
-  int n_norm_tiles;           // output tiles covered by the Q and K segments
+  float* sumsq;               // [T, n_norm_heads] or null
+  int n_norm_heads;           // 128-column blocks (heads) of the Q and K segments
   int* status;
 };
 
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = grow < p.T;
       const uint32_t tacc = tbase + lane_addr + acc * kBN;
       const float rs = row_ok ? p.row_scale[grow] : 0.f;
-      float ss = 0.f;
+      float ss = 0.f, ss_lo = 0.f;
       __nv_bfloat16* yrow = p.y + static_cast<size_t>(grow) * p.I + n0;
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
@@ -200,11 +200,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
+        if (c == 3) {  // first 128 columns (one head) done
+          ss_lo = ss;
+          ss = 0.f;
+        }
       }
       // The accumulator has been read: the MMA warp may reuse it for tile lt + 2.
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
-      if (row_ok && p.sumsq && nt < p.n_norm_tiles) p.sumsq[static_cast<size_t>(grow) * p.n_norm_tiles + nt] = ss;
+      if (row_ok && p.sumsq && 2 * nt < p.n_norm_heads) {
+        float* dst = p.sumsq + static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt;
+        dst[0] = ss_lo;
+        dst[1] = ss;
+      }
     }
   }
   tc_fence_before();
@@ -212,6 +220,232 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, 2 * kBN);
+  }
+}
+
+// ---------------------------------------------------------------- MX-32 block-scaled mode
+// Scale factors (UE8M0, one per 32 contraction elements) are re-tiled once into the tcgen05 scale
+// atom: for every 128-element k-block and 128-row block, 512 bytes where the byte for row
+// r = 32*m1 + m0 and k-sub-block j (0..3) sits at m0*16 + m1*4 + j. A 32 x 16-byte atom is copied
+// to TMEM with tcgen05.cp.32x128b.warpx4, giving lane m0 (in every quadrant) four 32-bit columns,
+// column m1 holding the four k-sub-block scales of row 32*m1 + m0; the MMA's sf_id picks the byte.
+// Tiled order: [k-block][128-row block][512 B], so the atoms of consecutive row blocks at one
+// k-block are adjacent (a 256-column B tile's two atoms are one 1 KB copy).
+constexpr uint32_t kSfAtomBytes = 512;
+
+__global__ void mx_pack_scales_kernel(const uint8_t* __restrict__ sf, int rows, int kblk32, int row_blocks,
+                                      uint8_t* __restrict__ out) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // one output byte
+  const int kb4 = kblk32 / 4;
+  const long long total = static_cast<long long>(kb4) * row_blocks * kSfAtomBytes;
+  if (idx >= total) return;
+  const int within = static_cast<int>(idx % kSfAtomBytes);
+  const long long atom = idx / kSfAtomBytes;
+  const int rb = static_cast<int>(atom % row_blocks);
+  const int kb = static_cast<int>(atom / row_blocks);
+  const int m0 = within >> 4, m1 = (within >> 2) & 3, j = within & 3;
+  const int r = rb * 128 + m1 * 32 + m0;
+  out[idx] = r < rows ? sf[static_cast<size_t>(r) * kblk32 + kb * 4 + j] : static_cast<uint8_t>(127);
+}
+
+constexpr int kMxStages = 4;
+constexpr uint32_t kMxSfaBytes = kSfAtomBytes;      // 128 rows of A
+constexpr uint32_t kMxSfbBytes = 2 * kSfAtomBytes;  // 256 rows of B
+// Stage = A tile, B tile, then the scale atoms, padded to 1 KB so every stage's A/B tiles keep the
+// 1024-byte alignment the 128-byte swizzle pattern is defined on.
+constexpr uint32_t kMxStageBytes = (kABytes + kBBytes + kMxSfaBytes + kMxSfbBytes + 1023) / 1024 * 1024;
+constexpr uint32_t kMxSmemBar = kMxStages * kMxStageBytes;
+constexpr uint32_t kMxSmemBytes = kMxSmemBar + 256 + 1024;
+constexpr uint32_t kMxColSf = kBN;  // scale columns follow the single accumulator: 12 per stage
+
+struct MxParams {
+  int T, I, H;
+  int m_tiles, n_tiles;
+  const uint8_t* sfa;  // tiled [H/128][m_tiles][512]
+  const uint8_t* sfb;  // tiled [H/128][I/128][512]
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* y;
+  float* sumsq;
+  int n_norm_heads;
+  int* status;
+};
+
+VOMNI_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Persistent like the ROW kernel, with one 256-column accumulator (TMEM also holds the staged
+// scale factors); the epilogue releases the accumulator as soon as it sits in registers.
+constexpr int kMxThreads = 320;  // TMA warp, MMA warp, eight epilogue warps
+
+__global__ void __launch_bounds__(kMxThreads, 1)
+    qkv_gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const MxParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kMxSmemBar);
+  uint64_t* empty = full + kMxStages;
+  uint64_t* acc_full = empty + kMxStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = p.H / kBK;
+  const int n_all = p.m_tiles * p.n_tiles;
+  const int n128 = p.I / 128;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kMxStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 256);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x) {
+        const int mb = tile / p.n_tiles;
+        const int nb = tile % p.n_tiles;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kMxStages;
+          const uint32_t ph = (it / kMxStages) & 1;
+          if (it >= kMxStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x41)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * kMxStageBytes;
+          mbar_expect_tx(&full[st], kABytes + kBBytes + kMxSfaBytes + kMxSfbBytes);
+          tma_load_2d(&tmA, &full[st], sa, kb * kBK, mb * kBM);
+          tma_load_2d(&tmB, &full[st], sa + kABytes, kb * kBK, nb * kBN);
+          bulk_g2s(sa + kABytes + kBBytes, p.sfa + (static_cast<size_t>(kb) * p.m_tiles + mb) * kSfAtomBytes,
+                   kMxSfaBytes, &full[st]);
+          bulk_g2s(sa + kABytes + kBBytes + kMxSfaBytes,
+                   p.sfb + (static_cast<size_t>(kb) * n128 + nb * 2) * kSfAtomBytes, kMxSfbBytes, &full[st]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128);
+      // scale atoms: 32 rows of 16 bytes, no swizzle; 8-row core matrices 128 B apart
+      const uint64_t sf_desc0 = make_sdesc(smem_u32(smem + kABytes + kBBytes), 16, 128, 0);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x, ++lt) {
+        if (lt >= 1 && !mbar_wait(acc_empty, (lt - 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x44)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kMxStages;
+          const uint32_t ph = (it / kMxStages) & 1;
+          if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x42)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t sdesc = sf_desc0 + ((st * kMxStageBytes) >> 4);
+          const uint32_t t_sfa = tbase + kMxColSf + st * 12;
+          const uint32_t t_sfb = t_sfa + 4;
+          tmem_cp_32x128b_warpx4(t_sfa, sdesc);
+          tmem_cp_32x128b_warpx4(t_sfb, sdesc + (kMxSfaBytes >> 4));
+          tmem_cp_32x128b_warpx4(t_sfb + 4, sdesc + ((kMxSfaBytes + kSfAtomBytes) >> 4));
+          const uint64_t ad0 = a_desc0 + ((st * kMxStageBytes) >> 4);
+          const uint64_t bd0 = ad0 + (kABytes >> 4);
+#pragma unroll
+          for (int k4 = 0; k4 < kBK / 32; ++k4)
+            // the scale byte (k-block within the 128-wide stage) sits in both the instruction
+            // descriptor and bits 30-31 of the scale-factor TMEM addresses
+            mma_mxf8_ss(tbase, ad0 + k4 * 2, bd0 + k4 * 2, idesc_mxf8(kBM, kBN, k4), (kb > 0 || k4 > 0) ? 1u : 0u,
+                        t_sfa | (static_cast<uint32_t>(k4) << 30), t_sfb | (static_cast<uint32_t>(k4) << 30));
+          tc_commit(&empty[st]);
+        }
+        if (ok) tc_commit(acc_full);
+      }
+    }
+  } else {
+    // Eight epilogue warps: two per TMEM lane quadrant, each owning 128 of the 256 columns. A warp
+    // drains its half of the accumulator into registers (bias added, rounded to bf16), releases the
+    // accumulator to the MMA warp, and only then stores, so the stores overlap the next tile's MMAs.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < n_all; tile += gridDim.x, ++lt) {
+      if (!mbar_wait(acc_full, lt & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x43)) break;
+      tc_fence_after();
+      const int m0 = (tile / p.n_tiles) * kBM;
+      const int nt = tile % p.n_tiles;
+      const int n0 = nt * kBN + half * 128;
+      const int grow = m0 + row;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + lane_addr + half * 128 + c * 32, r);
+        tmem_ld_wait(r);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (p.bias) {
+          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 bb = b4[i];
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(b2[j]);
+              v[8 * i + 2 * j] += f.x;
+              v[8 * i + 2 * j + 1] += f.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
+        ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+      }
+      if (grow < p.T) {
+        uint4* dst = reinterpret_cast<uint4*>(p.y + static_cast<size_t>(grow) * p.I + n0);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+      if (p.sumsq && grow < p.T && 2 * nt + half < p.n_norm_heads)
+        p.sumsq[static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt + half] = ss;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
   }
 }
 
@@ -230,17 +464,18 @@ __global__ void unpack_rows_kernel(const uint8_t* __restrict__ packed, int T, in
 // One CTA per token; a thread handles 8 consecutive lanes of one head's low half and the matching
 // 8 lanes of its high half.
 __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ y, int T, int I, int q_heads, int kv_heads,
-                                    const float* __restrict__ sumsq, int n_norm_tiles, int q_tiles, float eps,
+                                    const float* __restrict__ sumsq, float eps,
                                     const __nv_bfloat16* __restrict__ gamma_q, const __nv_bfloat16* __restrict__ gamma_k,
                                     const float* __restrict__ cos, const float* __restrict__ sin) {
   const int t = blockIdx.x;
   if (t >= T) return;
   __shared__ float inv_s[2];
   if (threadIdx.x < 2) {
-    const int lo = threadIdx.x == 0 ? 0 : q_tiles;
-    const int hi = threadIdx.x == 0 ? q_tiles : n_norm_tiles;
+    const int n_norm = q_heads + kv_heads;  // one partial per head
+    const int lo = threadIdx.x == 0 ? 0 : q_heads;
+    const int hi = threadIdx.x == 0 ? q_heads : n_norm;
     float s = 0.f;
-    for (int i = lo; i < hi; ++i) s += sumsq[static_cast<size_t>(t) * n_norm_tiles + i];
+    for (int i = lo; i < hi; ++i) s += sumsq[static_cast<size_t>(t) * n_norm + i];
     const int n = threadIdx.x == 0 ? q_heads : kv_heads;
     inv_s[threadIdx.x] = n > 0 ? rsqrtf(s / static_cast<float>(n * 128) + eps) : 1.f;
   }
@@ -354,7 +589,7 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.y = static_cast<__nv_bfloat16*>(y);
   p.sumsq = sumsq;
-  p.n_norm_tiles = (q_dim + kv_dim) / qkv::kBN;
+  p.n_norm_heads = (q_dim + kv_dim) / 128;
   p.m_tiles = (t + qkv::kBM - 1) / qkv::kBM;
   p.n_tiles = i / qkv::kBN;
   p.status = device_status_ptr();
@@ -376,14 +611,74 @@ extern "C" int vomni_qk_norm_rope(void* y, int t, int i, int q_heads, int kv_hea
   if (!y || !sumsq) return VOMNI_EINVAL;
   if (head_dim != 128 || t <= 0 || q_heads < 0 || kv_heads < 0) return VOMNI_EBADSHAPE;
   const int q_dim = q_heads * 128, kv_dim = kv_heads * 128;
-  if (q_dim + kv_dim > i || (q_dim % qkv::kBN) || (kv_dim % qkv::kBN)) return VOMNI_EBADSHAPE;
+  if (q_dim + kv_dim > i) return VOMNI_EBADSHAPE;
   if ((cos == nullptr) != (sin == nullptr)) return VOMNI_EINVAL;
   const uintptr_t al = reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(gamma_q) |
                        reinterpret_cast<uintptr_t>(gamma_k);
   if (al & 15 || (i % 8)) return VOMNI_EALIGN;
   qkv::qk_norm_rope_kernel<<<t, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(y), t, i, q_heads, kv_heads, sumsq, (q_dim + kv_dim) / qkv::kBN, q_dim / qkv::kBN,
-      eps, static_cast<const __nv_bfloat16*>(gamma_q), static_cast<const __nv_bfloat16*>(gamma_k), cos, sin);
+      static_cast<__nv_bfloat16*>(y), t, i, q_heads, kv_heads, sumsq, eps, static_cast<const __nv_bfloat16*>(gamma_q), static_cast<const __nv_bfloat16*>(gamma_k), cos, sin);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+extern "C" size_t vomni_mx_packed_scales_bytes(int rows, int k) {
+  if (rows <= 0 || k <= 0 || (k % 128)) return 0;
+  return static_cast<size_t>(k / 128) * ((rows + 127) / 128) * qkv::kSfAtomBytes;
+}
+
+extern "C" int vomni_mx_pack_scales(const void* sf, int rows, int k, void* out, vomni_stream_t stream) {
+  if (!sf || !out) return VOMNI_EINVAL;
+  const size_t bytes = vomni_mx_packed_scales_bytes(rows, k);
+  if (!bytes) return VOMNI_EBADSHAPE;
+  if (reinterpret_cast<uintptr_t>(out) & 15) return VOMNI_EALIGN;
+  const int threads = 256;
+  const long long blocks = (static_cast<long long>(bytes) + threads - 1) / threads;
+  qkv::mx_pack_scales_kernel<<<static_cast<unsigned>(blocks), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(sf), rows, k / 32, (rows + 127) / 128, static_cast<uint8_t*>(out));
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+extern "C" int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed, const void* w_codes,
+                                   const void* w_sf_packed, const void* bias, int t, int h, int i, int q_dim, int kv_dim,
+                                   void* y, float* sumsq, vomni_stream_t stream) {
+  if (!x_codes || !x_sf_packed || !w_codes || !w_sf_packed || !y) return VOMNI_EINVAL;
+  if (t <= 0 || h <= 0 || i <= 0 || (h % qkv::kBK) || (i % qkv::kBN)) return VOMNI_EBADSHAPE;
+  if (q_dim < 0 || kv_dim < 0 || q_dim + kv_dim > i || (q_dim % qkv::kBN) || (kv_dim % qkv::kBN)) return VOMNI_EBADSHAPE;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(x_codes) | reinterpret_cast<uintptr_t>(w_codes) |
+                       reinterpret_cast<uintptr_t>(x_sf_packed) | reinterpret_cast<uintptr_t>(w_sf_packed) |
+                       reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(y);
+  if (al & 15) return VOMNI_EALIGN;
+  int rc = require_sm100();
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  rc = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_codes, h, t, h, qkv::kBK, qkv::kBM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, qkv::kBN);
+  if (rc) return rc;
+  qkv::MxParams p;
+  p.T = t;
+  p.I = i;
+  p.H = h;
+  p.m_tiles = (t + qkv::kBM - 1) / qkv::kBM;
+  p.n_tiles = i / qkv::kBN;
+  p.sfa = static_cast<const uint8_t*>(x_sf_packed);
+  p.sfb = static_cast<const uint8_t*>(w_sf_packed);
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.sumsq = sumsq;
+  p.n_norm_heads = (q_dim + kv_dim) / 128;
+  p.status = device_status_ptr();
+  static bool attr = false;
+  if (!attr) {
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        qkv::kMxSmemBytes));
+    attr = true;
+  }
+  const int n_all = p.m_tiles * p.n_tiles;
+  const int grid = n_all < num_sms() ? n_all : num_sms();
+  qkv::qkv_gemm_mx_kernel<<<grid, qkv::kMxThreads, qkv::kMxSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }

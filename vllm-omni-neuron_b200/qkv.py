@@ -23,7 +23,6 @@ import torch
 
 from . import _lib
 
-_BN = 256
 
 
 def repack_mx_contiguous(w3: torch.Tensor) -> torch.Tensor:
@@ -47,6 +46,34 @@ def quantize_qkv_weight(w: torch.Tensor, q_size: int, kv_size: int):
     return codes.t().contiguous().to(torch.float8_e4m3fn), chan
 
 
+def pack_mx_scales(scales: torch.Tensor) -> torch.Tensor:
+    """UE8M0 scales ``[rows, k/32]`` (row-major, as ``adaln_modulate(quant="mx32")`` emits them) ->
+    the tcgen05 scale-atom tiling the block-scaled GEMM streams (``vomni_mx_pack_scales``)."""
+    rows, kb = scales.shape[-2] if scales.dim() > 1 else 1, scales.shape[-1]
+    sc = scales.reshape(-1, kb).contiguous()
+    rows = sc.shape[0]
+    L = _lib.load()
+    nbytes = L.vomni_mx_packed_scales_bytes(rows, kb * 32)
+    if nbytes == 0:
+        raise ValueError(f"MX-32 scales need k % 128 == 0, got k = {kb * 32}")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=sc.device)
+    _lib.check(L.vomni_mx_pack_scales(sc.data_ptr(), rows, kb * 32, out.data_ptr(),
+                                      torch.cuda.current_stream(sc.device).cuda_stream), "vomni_mx_pack_scales")
+    return out
+
+
+def quantize_qkv_weight_mx32(w: torch.Tensor):
+    """MX-32 quantisation of a fused ``[H, I]`` weight along the contraction (one UE8M0 scale per 32
+    consecutive H values of every output channel, the ``_mx_dequant`` format,
+    adaln_quant_torch.py:151-175). Returns (codes ``[I, H]`` fp8, scales ``[I, H/32]`` uint8,
+    packed scales for the GEMM)."""
+    from .adaln import adaln_modulate
+
+    codes, scales = adaln_modulate(w.t().contiguous().to(torch.bfloat16), None, None, eps=0.0, norm_type="none",
+                                   quant="mx32")
+    return codes, scales, pack_mx_scales(scales)
+
+
 def _wants_across_heads_norm(cfg) -> bool:
     if cfg is None or cfg is False:
         return False
@@ -57,6 +84,37 @@ def _wants_across_heads_norm(cfg) -> bool:
         if v is not None and "ACROSS_HEADS" not in str(getattr(v, "name", v)).upper():
             raise NotImplementedError(f"only RMS_NORM_ACROSS_HEADS qk-norm is implemented, got {v}")
     return True
+
+
+def _apply_norm_rope(y, T, I, num_heads, num_kv_heads, head_dim, sumsq, norm, rope, cfg, norm_eps, gamma_q, gamma_k,
+                     cos_cache, sin_cache, st):
+    """Across-heads RMS norm (+ gamma) and rotate-half RoPE on the Q/K segments of y, in place."""
+    if norm:
+        eps = float(getattr(cfg, "eps", norm_eps) or norm_eps)
+    else:
+        # RoPE without the across-heads norm: inv = 1 via a zero sum and eps = 1.
+        sumsq.zero_()
+        eps = 1.0
+    gq = gamma_q.reshape(-1).to(torch.bfloat16).contiguous() if (norm and gamma_q is not None) else None
+    gk = gamma_k.reshape(-1).to(torch.bfloat16).contiguous() if (norm and gamma_k is not None) else None
+    cs = sn = None
+    if rope:
+        if cos_cache is None or sin_cache is None:
+            raise ValueError("fused_rope needs cos_cache and sin_cache")
+        cs = cos_cache.reshape(-1, head_dim).float().contiguous()
+        sn = sin_cache.reshape(-1, head_dim).float().contiguous()
+        if cs.shape[0] != T:
+            if cs.shape[0] * (T // cs.shape[0]) == T:  # per-position caches shared across the batch
+                cs = cs.repeat(T // cs.shape[0], 1)
+                sn = sn.repeat(T // sn.shape[0], 1)
+            else:
+                raise ValueError(f"cos/sin caches have {cs.shape[0]} rows for {T} tokens")
+    ptr = lambda t: t.data_ptr() if t is not None else None
+    _lib.check(
+        _lib.load().vomni_qk_norm_rope(y.data_ptr(), T, I, num_heads, num_kv_heads, head_dim, sumsq.data_ptr(), eps,
+                                       ptr(gq), ptr(gk), ptr(cs), ptr(sn), st),
+        "vomni_qk_norm_rope",
+    )
 
 
 def row_mx_qkv_proj(
@@ -119,7 +177,7 @@ def row_mx_qkv_proj(
     rope = bool(fused_rope)
     sumsq = None
     if norm or rope:
-        sumsq = torch.empty(T, (q_dim + kv_dim) // _BN, dtype=torch.float32, device=dev)
+        sumsq = torch.empty(T, (q_dim + kv_dim) // head_dim, dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev).cuda_stream
     _lib.check(
         L.vomni_qkv_fp8_gemm(codes.data_ptr(), row_scale.data_ptr(), weight.contiguous().data_ptr(), chan.data_ptr(),
@@ -128,30 +186,57 @@ def row_mx_qkv_proj(
         "vomni_qkv_fp8_gemm",
     )
     if norm or rope:
-        if norm:
-            eps = float(getattr(qk_norm_pre_rope, "eps", norm_eps) or norm_eps)
-        else:
-            # RoPE without the across-heads norm: inv = 1 via a zero sum and eps = 1.
-            sumsq.zero_()
-            eps = 1.0
-        gq = qk_norm_pre_rope_q_gamma.reshape(-1).to(torch.bfloat16).contiguous() if (norm and qk_norm_pre_rope_q_gamma is not None) else None
-        gk = qk_norm_pre_rope_k_gamma.reshape(-1).to(torch.bfloat16).contiguous() if (norm and qk_norm_pre_rope_k_gamma is not None) else None
-        cs = sn = None
-        if rope:
-            if cos_cache is None or sin_cache is None:
-                raise ValueError("fused_rope needs cos_cache and sin_cache")
-            cs = cos_cache.reshape(-1, head_dim).float().contiguous()
-            sn = sin_cache.reshape(-1, head_dim).float().contiguous()
-            if cs.shape[0] != T:
-                if cs.shape[0] * (T // cs.shape[0]) == T:  # per-position caches shared across the batch
-                    cs = cs.repeat(T // cs.shape[0], 1)
-                    sn = sn.repeat(T // sn.shape[0], 1)
-                else:
-                    raise ValueError(f"cos/sin caches have {cs.shape[0]} rows for {T} tokens")
-        ptr = lambda t: t.data_ptr() if t is not None else None
-        _lib.check(
-            L.vomni_qk_norm_rope(y.data_ptr(), T, I, num_heads, num_kv_heads, head_dim, sumsq.data_ptr(), eps, ptr(gq),
-                                 ptr(gk), ptr(cs), ptr(sn), st),
-            "vomni_qk_norm_rope",
-        )
+        _apply_norm_rope(y, T, I, num_heads, num_kv_heads, head_dim, sumsq, norm, rope, qk_norm_pre_rope, norm_eps,
+                         qk_norm_pre_rope_q_gamma, qk_norm_pre_rope_k_gamma, cos_cache, sin_cache, st)
+    return y
+
+
+def mx32_qkv_proj(
+    x,
+    w_codes: torch.Tensor,
+    w_scales_packed: torch.Tensor,
+    bias: torch.Tensor | None,
+    *,
+    num_heads: int,
+    head_dim: int,
+    num_kv_heads: int,
+    fused_rope: bool = False,
+    cos_cache: torch.Tensor | None = None,
+    sin_cache: torch.Tensor | None = None,
+    qk_norm_pre_rope=None,
+    qk_norm_pre_rope_q_gamma: torch.Tensor | None = None,
+    qk_norm_pre_rope_k_gamma: torch.Tensor | None = None,
+    norm_eps: float = 1e-6,
+) -> torch.Tensor:
+    """MX-32 variant of :func:`row_mx_qkv_proj`: ``x = (codes [..., H] fp8, scales [..., H/32] u8)``
+    from ``adaln_modulate(quant="mx32")``; weights from :func:`quantize_qkv_weight_mx32`. The GEMM is
+    a tcgen05 block-scaled MMA (UE8M0 per 32 elements on both operands); the epilogue (bias, across-heads
+    RMS norm, gamma, rotate-half RoPE) is the ROW path's."""
+    if head_dim != 128:
+        raise ValueError(f"head_dim must be 128, got {head_dim}")
+    codes, scales = x
+    lead = tuple(codes.shape[:-1])
+    H = codes.shape[-1]
+    dev = codes.device
+    T = codes.numel() // H
+    I = w_codes.shape[0]
+    q_dim, kv_dim = num_heads * head_dim, num_kv_heads * head_dim
+    assert q_dim + 2 * kv_dim == I and w_codes.shape[1] == H
+    L = _lib.load()
+    xs = pack_mx_scales(scales.reshape(T, H // 32))
+    b = bias.reshape(-1).to(torch.bfloat16).contiguous() if bias is not None else None
+    y = torch.empty(lead + (I,), dtype=torch.bfloat16, device=dev)
+    norm = _wants_across_heads_norm(qk_norm_pre_rope)
+    rope = bool(fused_rope)
+    sumsq = torch.empty(T, (q_dim + kv_dim) // head_dim, dtype=torch.float32, device=dev) if (norm or rope) else None
+    st = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(
+        L.vomni_qkv_mx32_gemm(codes.contiguous().data_ptr(), xs.data_ptr(), w_codes.contiguous().data_ptr(),
+                              w_scales_packed.data_ptr(), b.data_ptr() if b is not None else None, T, H, I, q_dim,
+                              kv_dim, y.data_ptr(), sumsq.data_ptr() if sumsq is not None else None, st),
+        "vomni_qkv_mx32_gemm",
+    )
+    if norm or rope:
+        _apply_norm_rope(y, T, I, num_heads, num_kv_heads, head_dim, sumsq, norm, rope, qk_norm_pre_rope, norm_eps,
+                         qk_norm_pre_rope_q_gamma, qk_norm_pre_rope_k_gamma, cos_cache, sin_cache, st)
     return y
