@@ -58,6 +58,11 @@ VOMNI_API int vomni_device_status(int* code, int clear);
  * word reads VOMNI_DEV_TIMEOUT_BASE + 0x7F and *result_host = 0 (1 would mean the wait
  * completed). Synchronises `stream`. */
 VOMNI_API int vomni_selftest_bounded_wait(unsigned budget_us, int* result_host, vomni_stream_t stream);
+/* Stream-ordered 2-D copy (height rows of width bytes; pitches in bytes) between any two of host
+ * (pinned) and device memory: the host-resident attention entry streams head groups with it.
+ * No counterpart in the reference (its inputs are always device-resident). */
+VOMNI_API int vomni_memcpy_2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                                    size_t height, vomni_stream_t stream);
 
 /* ------------------------------------------------------------------ const-max attention
  * Replaces the NKI kernel ring_attention_const_max_fwd

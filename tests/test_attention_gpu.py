@@ -162,3 +162,25 @@ def test_errors(pkg, dev):
         pkg.ring_attention_const_max_fwd(q[..., :64].contiguous(), k[..., :64].contiguous(), v[..., :64].contiguous())
     with pytest.raises(TypeError):
         pkg.ring_attention_const_max_fwd(q.float(), k, v)
+
+
+@pytest.mark.parametrize("b,s,h,training,layout", [(1, 1000, 12, False, "bhds"), (2, 777, 7, True, "bhsd")])
+def test_host_streamed_equals_device(pkg, dev, b, s, h, training, layout):
+    """Pinned host q/k/v stream through head groups; heads are independent, so the host result is
+    bit-identical to the device-resident call."""
+    g = torch.Generator().manual_seed(11)
+    q, k, v = ((torch.randn(b, s, h, 128, generator=g) * 0.5).to(torch.bfloat16) for _ in range(3))
+    attn = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.attention")
+    host = attn.ring_attention_const_max_fwd(q.pin_memory(), k.pin_memory(), v.pin_memory(), training=training,
+                                             out_layout=layout)
+    devr = attn.ring_attention_const_max_fwd(q.to(dev), k.to(dev), v.to(dev), training=training, out_layout=layout)
+    torch.cuda.synchronize()
+    if training:
+        assert host[0].device.type == "cpu" and torch.equal(host[0], devr[0].cpu())
+        assert torch.equal(host[1], devr[1].cpu())
+    else:
+        assert host.device.type == "cpu" and torch.equal(host, devr.cpu())
+    wan = pkg.wan_cp_self_attention(q.pin_memory(), k.pin_memory(), v.pin_memory(), 128 ** -0.5, 1, None, None)
+    assert torch.equal(wan, pkg.wan_cp_self_attention(q.to(dev), k.to(dev), v.to(dev), 128 ** -0.5, 1, None, None).cpu())
+    with pytest.raises(ValueError):
+        attn.ring_attention_const_max_fwd(q, k, v)  # host tensors must be pinned

@@ -13,6 +13,13 @@
 
 All compute runs in ``libvomni_b200.so`` (sm_100a). There is no fallback path: a missing library or
 a non-sm_100 device raises.
+
+Host-resident inputs (B200 extension): when q, k and v are pinned CPU tensors, both entry points
+stream them to the current CUDA device in head groups — the copy of group i+1 (copy engine, 2-D
+strided copies straight out of the token-major host layout) overlaps the attention of group i, and
+the result of group i returns to pinned host memory while group i+1 computes. Heads are
+independent, so the result is identical to the device-resident call; the output is a pinned CPU
+tensor, complete on return.
 """
 
 from __future__ import annotations
@@ -57,6 +64,81 @@ def token_major(t: torch.Tensor) -> tuple[torch.Tensor, int]:
     if ok:
         return t, st[1]
     return t.contiguous(), h * d
+
+
+_HOST_GROUP_HEADS = 5
+_AUX_STREAMS: dict = {}
+
+
+def _aux_streams(dev: torch.device):
+    """(host->device copy stream, device->host copy stream, second compute stream) of a device."""
+    key = dev.index
+    if key not in _AUX_STREAMS:
+        _AUX_STREAMS[key] = tuple(torch.cuda.Stream(dev) for _ in range(3))
+    return _AUX_STREAMS[key]
+
+
+def _copy_2d(dst_ptr, dpitch, src_ptr, spitch, width, height, stream):
+    _lib.check(_lib.load().vomni_memcpy_2d_async(dst_ptr, dpitch, src_ptr, spitch, width, height, stream.cuda_stream),
+               "vomni_memcpy_2d_async")
+
+
+def _host_streamed(fn, q, k, v, *, out_layout: str, training: bool, alternate: bool = True,
+                   group_heads: int | None = None):
+    """Run ``fn(q_dev, k_dev, v_dev) -> out | (out, lse)`` over head groups of pinned host q/k/v.
+
+    Group g's host->device copies run on a copy stream, its attention alternates between the
+    caller's stream and a second compute stream (so one group's tail wave overlaps the next group;
+    ``alternate=False`` keeps every group on the caller's stream, as a ring context's buffers
+    require), and its output returns on a second copy stream. Returns pinned host tensors."""
+    b, s, h, d = q.shape
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.device.type != "cpu" or not t.is_pinned():
+            raise ValueError(f"host-resident {name} must be a pinned CPU tensor (tensor.pin_memory())")
+        if t.dtype != torch.bfloat16 or tuple(t.shape) != (b, s, h, d):
+            raise TypeError(f"{name} must be bfloat16 [b, s, h, d] like q")
+    q, k, v = (t if t.is_contiguous() else t.contiguous().pin_memory() for t in (q, k, v))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    main = torch.cuda.current_stream(dev)
+    h2d, d2h, alt = _aux_streams(dev)
+    esz = 2
+    dq, dk, dv = (torch.empty((b, s, h, d), dtype=torch.bfloat16, device=dev) for _ in range(3))
+    o_shape = (b, h, d, s) if out_layout == "bhds" else (b, h, s, d)
+    host_o = torch.empty(o_shape, dtype=torch.bfloat16, pin_memory=True)
+    n_lse = 128 * (-(-s // 128))
+    host_lse = torch.empty((b, h, 128, n_lse // 128), dtype=torch.float32, pin_memory=True) if training else None
+    gh = max(1, int(group_heads or _HOST_GROUP_HEADS))
+    row = h * d * esz
+    h2d.wait_stream(main)
+    alt.wait_stream(main)
+    keep = []
+    for gi, h0 in enumerate(range(0, h, gh)):
+        h1 = min(h, h0 + gh)
+        w = (h1 - h0) * d * esz
+        for src, dst in ((q, dq), (k, dk), (v, dv)):
+            _copy_2d(dst.data_ptr() + h0 * d * esz, row, src.data_ptr() + h0 * d * esz, row, w, b * s, h2d)
+        arrived = torch.cuda.Event()
+        arrived.record(h2d)
+        cs = alt if (alternate and gi % 2) else main
+        cs.wait_event(arrived)
+        with torch.cuda.stream(cs):
+            res = fn(dq[:, :, h0:h1], dk[:, :, h0:h1], dv[:, :, h0:h1])
+        o, lse = res if training else (res, None)
+        done = torch.cuda.Event()
+        done.record(cs)
+        d2h.wait_event(done)
+        per_head = o[0, 0].numel() * esz
+        _copy_2d(host_o.data_ptr() + h0 * per_head, h * per_head, o.data_ptr(), (h1 - h0) * per_head,
+                 (h1 - h0) * per_head, b, d2h)
+        if training:
+            lh = 128 * (n_lse // 128) * 4
+            _copy_2d(host_lse.data_ptr() + h0 * lh, h * lh, lse.data_ptr(), (h1 - h0) * lh, (h1 - h0) * lh, b, d2h)
+        keep.append(res)
+    d2h.synchronize()  # every group's copy-out waited for its compute, which waited for its copy-in
+    main.wait_stream(alt)
+    main.wait_stream(d2h)
+    del keep
+    return (host_o, host_lse) if training else host_o
 
 
 def _stream_ptr(dev: torch.device) -> int:
@@ -126,7 +208,17 @@ def ring_attention_const_max_fwd(
 
     ``group`` (B200 addition): the ``torch.distributed`` process group of this rank's ring when
     ``num_workers > 1``; defaults to the group matching ``replica_groups`` (built once per ring).
+    Pinned host q/k/v are streamed by head groups (module docstring) and give host results.
     """
+    if q.device.type == "cpu" and k.device.type == "cpu" and v.device.type == "cpu":
+        assert q.dim() == 4 and q.shape[-1] == _HEAD_DIM, "q, k, v must be token-major [b, seqlen, h, 128]"
+
+        def dev_call(qd, kd, vd):
+            return ring_attention_const_max_fwd(qd, kd, vd, replica_groups, num_workers, softmax_scale, training,
+                                                torch.float32, kv_prefetch_depth, group=group, out_layout=out_layout)
+
+        res = _host_streamed(dev_call, q, k, v, out_layout=out_layout, training=training, alternate=num_workers <= 1)
+        return (res[0], res[1].to(lse_dtype)) if training else res
     _check_qkv(q, k, v)
     if num_workers <= 1:
         res = attention_local(q, k, v, softmax_scale, out_layout=out_layout, training=training)

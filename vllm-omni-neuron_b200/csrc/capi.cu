@@ -183,3 +183,13 @@ extern "C" int vomni_selftest_bounded_wait(unsigned budget_us, int* result_host,
   VOMNI_CUDA_TRY(e);
   return VOMNI_OK;
 }
+
+extern "C" int vomni_memcpy_2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                                     size_t height, vomni_stream_t stream) {
+  if (!dst || !src) return VOMNI_EINVAL;
+  if (width > dpitch || width > spitch) return VOMNI_EBADSHAPE;
+  if (width == 0 || height == 0) return VOMNI_OK;
+  VOMNI_CUDA_TRY(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDefault,
+                                   reinterpret_cast<cudaStream_t>(stream)));
+  return VOMNI_OK;
+}
