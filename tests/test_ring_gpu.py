@@ -50,6 +50,10 @@ def _worker(rank, world, port, shapes, out_q):
                 o, lse = pkg.ring_attention_const_max_fwd(q, k, v, num_workers=world, training=True)
                 od = pkg.wan_cp_self_attention(q, k, v, 1 / math.sqrt(128), world, dist.group.WORLD, None)
             torch.cuda.synchronize()
+            # pinned host shards: head groups streamed through the ring, bit-identical to the device call
+            oh = pkg.wan_cp_self_attention(*(x.pin_memory() for x in shards[rank]), 1 / math.sqrt(128), world,
+                                           dist.group.WORLD, None)
+            errs.append(("host_equal", (b, s, h), float(oh.device.type == "cpu" and torch.equal(oh, od.cpu()))))
             f = lambda t: t.float().cpu().numpy()
             qs, ks, vs = ([f(sh[i]) for sh in shards] for i in range(3))
             ref_o, ref_l = oat.const_max_ring_attention(qs, ks, vs, training=True)
@@ -86,7 +90,9 @@ def test_ring_multi_gpu():
         assert tb is None, tb
         assert status == 0
         for name, shape, val in errs:
-            if name.startswith("cos"):
+            if name == "host_equal":
+                assert val == 1.0, (rank, name, shape)
+            elif name.startswith("cos"):
                 assert val >= 0.9999, (rank, name, shape, val)
             elif name == "max_lse":
                 assert val <= 3e-2, (rank, name, shape, val)
