@@ -45,7 +45,9 @@ constexpr uint32_t kSmemV = kSmemK + 2 * kTileBytes;    // 2 stages
 constexpr uint32_t kSmemBar = kSmemV + 2 * kTileBytes;  // barriers + scalars
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + alignment slack
 
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 11, TURN = 13, O_FULL = 15, NBAR = 16 };
+// S_FULL: one barrier per query tile t at index 2t. P_FULL: one per (tile t, key half h) at 2t + h;
+// the whole-tile pipeline uses only h = 0.
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 13, O_FULL = 17, NBAR = 18 };
 
 // TMEM columns: tile t owns S_t = [t*128, t*128+128) (P_t, bf16, aliases its first 64 columns) and
 // O_t = [256 + t*128, 256 + t*128 + 128).
@@ -80,6 +82,14 @@ __device__ __forceinline__ void issue_qk(uint32_t d_s, uint64_t q_desc, uint64_t
     mma_f16_ss(d_s, q_desc + off, k_desc + off, kIdescQK, kk > 0);
   }
 }
+// O_t += P_t V over keys [64*hf, 64*hf + 64).
+__device__ __forceinline__ void issue_pv_half(uint32_t d_o, uint32_t p_tmem, uint64_t v_desc, int hf, bool accumulate) {
+#pragma unroll
+  for (int k2 = 0; k2 < 4; ++k2) {
+    const int kk = hf * 4 + k2;
+    mma_f16_ts(d_o, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV, (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
 // O_t += P_t V: P from TMEM (8 columns of packed bf16 per 16 keys), V as an MN-major SW128 operand
 // (16 keys = two 8-row groups = +2048 B; the two 64-wide d halves are 16 KB apart).
 __device__ __forceinline__ void issue_pv(uint32_t d_o, uint32_t p_tmem, uint64_t v_desc, bool accumulate) {
@@ -110,6 +120,35 @@ VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], float scale_log2, float ne
   }
 }
 
+// Whole-tile softmax that publishes P in two halves: keys 0-63 (P columns 0-31) are signalled on
+// `p_lo` as soon as they are in TMEM, so the PV MMAs over them overlap the exponentials of keys
+// 64-127. The S columns 64-127 are loaded while keys 0-63 are computed.
+template <int kPoly, bool kMask>
+VOMNI_DEV void softmax_tile_split(uint32_t col_s, float scale_log2, float neg_c2, int valid, float (&acc)[4],
+                                  uint64_t* p_lo) {
+  uint32_t s0[32], s1[32], s2[32], s3[32];
+  tmem_ld32(col_s, s0);
+  tmem_ld32(col_s + 32, s1);
+  tmem_ld_wait(s0);
+  tmem_ld_wait(s1);
+  tmem_ld32(col_s + 64, s2);
+  tmem_ld32(col_s + 96, s3);
+  uint32_t pk[16];
+  softmax_chunk<kPoly, kMask>(s0, scale_log2, neg_c2, valid, acc, pk);
+  tmem_st16(col_s, pk);
+  softmax_chunk<kPoly, kMask>(s1, scale_log2, neg_c2, valid - 32, acc, pk);
+  tmem_st16(col_s + 16, pk);
+  tmem_st_wait();
+  tc_fence_before();
+  mbar_arrive(p_lo);
+  tmem_ld_wait(s2);
+  tmem_ld_wait(s3);
+  softmax_chunk<kPoly, kMask>(s2, scale_log2, neg_c2, valid - 64, acc, pk);
+  tmem_st16(col_s + 32, pk);
+  softmax_chunk<kPoly, kMask>(s3, scale_log2, neg_c2, valid - 96, acc, pk);
+  tmem_st16(col_s + 48, pk);
+}
+
 template <int kPoly, bool kMask>
 VOMNI_DEV void softmax_tile(uint32_t col_s, float scale_log2, float neg_c2, int valid, float (&acc)[4]) {
   // The whole 128-column S row is loaded with four back-to-back TMEM loads and one wait, so the
@@ -135,7 +174,14 @@ VOMNI_DEV void softmax_tile(uint32_t col_s, float scale_log2, float neg_c2, int 
   tmem_st16(col_s + 48, pk);
 }
 
-template <int kPoly, bool kPingPong>
+// K stage j%2 is free once S of the last query tile for step j is complete; V stage (j-1)%2 too
+// (its PV MMAs were issued before that QK). Replaces two tcgen05.commit per step on the MMA thread.
+VOMNI_DEV void release_stages(uint64_t* bars, int j) {
+  mbar_arrive(&bars[K_EMPTY + (j & 1)]);
+  if (j > 0) mbar_arrive(&bars[V_EMPTY + ((j - 1) & 1)]);
+}
+
+template <int kPoly, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     cm_attend_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -160,9 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars[K_EMPTY + i], 1);
       mbar_init(&bars[V_FULL + i], 1);
       mbar_init(&bars[V_EMPTY + i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bars[S_FULL + i], 1);
       mbar_init(&bars[P_FULL + i], 128);
-      mbar_init(&bars[TURN + i], 128);
     }
     mbar_init(&bars[O_FULL], 1);
     *abort_flag = 0;
@@ -222,25 +269,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         for (int t = 0; t < kQT; ++t) {
           issue_qk(tbase + kColS + t * 128, q_desc + t * kTileDesc, k_desc);
-          tc_commit(&bars[S_FULL + t]);
+          tc_commit(&bars[S_FULL + 2 * t]);
         }
-        tc_commit(&bars[K_EMPTY]);
       }
       for (int j = 1; ok && j <= n_tiles; ++j) {
         const int jj = j - 1;
         const int vs = jj & 1, ks = j & 1;
         for (int t = 0; t < kQT && ok; ++t) {
-          if (!mbar_wait(&bars[P_FULL + t], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) { ok = false; break; }
-          if (t == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(tbase + kColO + t * 128, tbase + kColS + t * 128, v_desc + vs * kTileDesc, jj > 0);
-          if (t == kQT - 1) tc_commit(&bars[V_EMPTY + vs]);
+          const uint32_t d_o = tbase + kColO + t * 128, d_s = tbase + kColS + t * 128;
+          if (kSplit) {
+            // PV over keys 0-63 as soon as that half of P is in TMEM, then keys 64-127; the next QK
+            // follows (it overwrites S/P, which these PV MMAs read: issue order suffices).
+            for (int hf = 0; hf < 2 && ok; ++hf) {
+              if (!mbar_wait(&bars[P_FULL + 2 * t + hf], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) { ok = false; break; }
+              if (t == 0 && hf == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) { ok = false; break; }
+              tc_fence_after();
+              issue_pv_half(d_o, d_s, v_desc + vs * kTileDesc, hf, jj > 0);
+            }
+            if (!ok) break;
+          } else {
+            if (!mbar_wait(&bars[P_FULL + 2 * t], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) { ok = false; break; }
+            if (t == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(d_o, d_s, v_desc + vs * kTileDesc, jj > 0);
+          }
           if (j < n_tiles) {
             if (t == 0 && !mbar_wait(&bars[K_FULL + ks], (j >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4)) { ok = false; break; }
             tc_fence_after();
-            issue_qk(tbase + kColS + t * 128, q_desc + t * kTileDesc, k_desc + ks * kTileDesc);
-            tc_commit(&bars[S_FULL + t]);
-            if (t == kQT - 1) tc_commit(&bars[K_EMPTY + ks]);
+            issue_qk(d_s, q_desc + t * kTileDesc, k_desc + ks * kTileDesc);
+            tc_commit(&bars[S_FULL + 2 * t]);
           }
         }
       }
@@ -265,25 +322,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       c = __bfloat162float(__float2bfloat16_rn(c32));
     }
     const float neg_c2 = -c * 1.4426950408889634f;
+    // One thread of the last tile's warpgroup frees the K/V stages: S_{last}(j) complete means
+    // every QK of step j (and, issued before it, every PV of step j-1) has finished reading them.
+    const bool releaser = (t == kQT - 1) && row == 0;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&bars[S_FULL + t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
-      // Ping-pong: tile 1's softmax of step j starts when tile 0's has finished it, and tile 0's
-      // softmax of step j waits for tile 1's of step j-1; each then runs while the tensor pipe does
-      // the other tile's PV and next QK, instead of both competing for the exp pipe at once.
-      if (kPingPong && t == 1 && !mbar_wait(&bars[TURN + 1], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 10)) { ok = false; break; }
-      if (kPingPong && t == 0 && j > 0 && !mbar_wait(&bars[TURN + 0], (j - 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 11)) { ok = false; break; }
-      tc_fence_after();
+    for (int j = 0; j < n_tiles && ok; ++j) {
       const int valid = p.n_keys - j * kTile;  // keys of this tile inside the pass's range
-      if (valid >= kTile)
-        softmax_tile<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc);
-      else
-        softmax_tile<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bars[P_FULL + t]);
-      if (kPingPong) mbar_arrive(&bars[TURN + (t ^ 1)]);
+      if (kSplit) {
+        if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+        tc_fence_after();
+        if (releaser) release_stages(bars, j);
+        if (valid >= kTile)
+          softmax_tile_split<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t]);
+        else
+          softmax_tile_split<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t]);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars[P_FULL + 2 * t + 1]);
+      } else {
+        if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+        tc_fence_after();
+        if (releaser) release_stages(bars, j);
+        if (valid >= kTile)
+          softmax_tile<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc);
+        else
+          softmax_tile<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars[P_FULL + 2 * t]);
+      }
     }
     const float rowsum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     // ---------------------------------------------------------- epilogue
@@ -491,19 +559,19 @@ extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void*
   p.status = device_status_ptr();
 
   // Tuning knobs (read once): VOMNI_CM_POLY = share of exponentials on the FMA pipe as 1/N
-  // (0 = none), VOMNI_CM_PINGPONG = 0/1.
-  static int poly = -1, pingpong = -1;
+  // (0 = none), VOMNI_CM_SPLIT = 1 to publish P in two key halves, 0 for whole tiles.
+  static int poly = -1, split = -1;
   if (poly < 0) {
     const char* e = getenv("VOMNI_CM_POLY");
     poly = e ? atoi(e) : 0;
-    const char* f = getenv("VOMNI_CM_PINGPONG");
-    pingpong = f ? atoi(f) : 0;
+    const char* f = getenv("VOMNI_CM_SPLIT");
+    split = f ? atoi(f) : 1;
   }
-  auto kern = cm::cm_attend_kernel<0, true>;
-  if (poly == 2) kern = pingpong ? cm::cm_attend_kernel<2, true> : cm::cm_attend_kernel<2, false>;
-  else if (poly == 4) kern = pingpong ? cm::cm_attend_kernel<4, true> : cm::cm_attend_kernel<4, false>;
-  else if (poly == 8) kern = pingpong ? cm::cm_attend_kernel<8, true> : cm::cm_attend_kernel<8, false>;
-  else kern = pingpong ? cm::cm_attend_kernel<0, true> : cm::cm_attend_kernel<0, false>;
+  auto kern = cm::cm_attend_kernel<0, false>;
+  if (poly == 2) kern = split ? cm::cm_attend_kernel<2, true> : cm::cm_attend_kernel<2, false>;
+  else if (poly == 4) kern = split ? cm::cm_attend_kernel<4, true> : cm::cm_attend_kernel<4, false>;
+  else if (poly == 8) kern = split ? cm::cm_attend_kernel<8, true> : cm::cm_attend_kernel<8, false>;
+  else kern = split ? cm::cm_attend_kernel<0, true> : cm::cm_attend_kernel<0, false>;
   VOMNI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kSmemBytes));
   dim3 grid((s_q + cm::kTile * cm::kQT - 1) / (cm::kTile * cm::kQT), b * h);
   kern<<<grid, cm::kThreads, cm::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
