@@ -123,9 +123,20 @@ VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], float scale_log2, float ne
 // Whole-tile softmax that publishes P in two halves: keys 0-63 (P columns 0-31) are signalled on
 // `p_lo` as soon as they are in TMEM, so the PV MMAs over them overlap the exponentials of keys
 // 64-127. The S columns 64-127 are loaded while keys 0-63 are computed.
-template <int kPoly, bool kMask>
+// Signal that this thread's (or, for a CTA pair, this warp's) P columns are in TMEM.
+template <bool kPair>
+VOMNI_DEV void publish_p(uint64_t* bar, uint32_t bar_cluster) {
+  if (kPair) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(bar_cluster);
+  } else {
+    mbar_arrive(bar);
+  }
+}
+
+template <int kPoly, bool kMask, bool kPair>
 VOMNI_DEV void softmax_tile_split(uint32_t col_s, float scale_log2, float neg_c2, int valid, float (&acc)[4],
-                                  uint64_t* p_lo) {
+                                  uint64_t* p_lo, uint32_t p_lo_cluster) {
   uint32_t s0[32], s1[32], s2[32], s3[32];
   tmem_ld32(col_s, s0);
   tmem_ld32(col_s + 32, s1);
@@ -140,7 +151,7 @@ VOMNI_DEV void softmax_tile_split(uint32_t col_s, float scale_log2, float neg_c2
   tmem_st16(col_s + 16, pk);
   tmem_st_wait();
   tc_fence_before();
-  mbar_arrive(p_lo);
+  publish_p<kPair>(p_lo, p_lo_cluster);
   tmem_ld_wait(s2);
   tmem_ld_wait(s3);
   softmax_chunk<kPoly, kMask>(s2, scale_log2, neg_c2, valid - 64, acc, pk);
@@ -179,6 +190,122 @@ VOMNI_DEV void softmax_tile(uint32_t col_s, float scale_log2, float neg_c2, int 
 VOMNI_DEV void release_stages(uint64_t* bars, int j) {
   mbar_arrive(&bars[K_EMPTY + (j & 1)]);
   if (j > 0) mbar_arrive(&bars[V_EMPTY + ((j - 1) & 1)]);
+}
+
+// Softmax + epilogue warpgroups (warps 2..9): query tile t = (warp-2)/4, one query row per thread.
+// q_base: first query row of this CTA's tile 0; tile_stride: rows between its tiles. kPair: the P
+// barriers live in the pair leader and take one arrival per warp (p_full_cluster = their
+// shared::cluster address); otherwise they are local and take one arrival per thread.
+template <int kPoly, bool kSplit, bool kPair>
+VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort_flag, uint32_t tbase, int warp, int lane,
+                            int q_base, int tile_stride, int bh, int n_tiles, uint32_t p_full_cluster) {
+  const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+  const int quad = warp & 3;      // TMEM lane quadrant this warp may access
+  const int row = quad * 32 + lane;
+  const int grow = q_base + t * tile_stride + row;
+  const bool row_ok = grow < p.s_q;
+  const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+  const uint32_t col_s = tbase + lane_addr + kColS + t * 128;
+  const uint32_t col_o = tbase + lane_addr + kColO + t * 128;
+  const size_t rowidx = static_cast<size_t>(bh) * p.s_q + grow;
+  float c = 0.f;
+  if (row_ok) {
+    // c_i = scale * sqrt(kmax2 * ||q_i||^2), held in bf16 like the reference's c_row
+    // (ring_attention_const_max_fwd.py:585-591).
+    const float c32 = p.scale * sqrtf(p.kmax2[bh] * p.qn2[rowidx]);
+    c = __bfloat162float(__float2bfloat16_rn(c32));
+  }
+  const float neg_c2 = -c * 1.4426950408889634f;
+  // One thread of the last tile's warpgroup frees the K/V stages: S_{last}(j) complete means
+  // every QK of step j (and, issued before it, every PV of step j-1) has finished reading them.
+  const bool releaser = (t == kQT - 1) && row == 0;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  bool ok = true;
+  for (int j = 0; j < n_tiles && ok; ++j) {
+    const int valid = p.n_keys - j * kTile;  // keys of this tile inside the pass's range
+    if (kSplit) {
+      if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+      tc_fence_after();
+      if (releaser) release_stages(bars, j);
+      if (valid >= kTile)
+        softmax_tile_split<kPoly, false, kPair>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t],
+                                                p_full_cluster + (2 * t) * 8);
+      else
+        softmax_tile_split<kPoly, true, kPair>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t],
+                                               p_full_cluster + (2 * t) * 8);
+      tmem_st_wait();
+      tc_fence_before();
+      publish_p<kPair>(&bars[P_FULL + 2 * t + 1], p_full_cluster + (2 * t + 1) * 8);
+    } else {
+      if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+      tc_fence_after();
+      if (releaser) release_stages(bars, j);
+      if (valid >= kTile)
+        softmax_tile<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc);
+      else
+        softmax_tile<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[P_FULL + 2 * t]);
+    }
+  }
+  const float rowsum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  // ---------------------------------------------------------- epilogue
+  if (ok && mbar_wait(&bars[O_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) {
+    tc_fence_after();
+    const bool acc_in = p.flags & VOMNI_CM_ACC_IN;
+    const bool final_pass = p.flags & VOMNI_CM_FINAL;
+    float l = rowsum;
+    if (acc_in && row_ok) l += p.acc_l[rowidx];
+    const float inv = 1.f / fmaxf(l, 1e-37f);
+    float* acc_row = p.acc_o ? p.acc_o + rowidx * kD : nullptr;
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t o[32];
+      tmem_ld32(col_o + ch * 32, o);
+      tmem_ld_wait(o);
+      if (!row_ok) continue;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]);
+      if (acc_in) {
+        const float4* src = reinterpret_cast<const float4*>(acc_row + ch * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 a = src[i];
+          v[4 * i] += a.x; v[4 * i + 1] += a.y; v[4 * i + 2] += a.z; v[4 * i + 3] += a.w;
+        }
+      }
+      if (!final_pass) {
+        float4* dst = reinterpret_cast<float4*>(acc_row + ch * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else if (p.flags & VOMNI_CM_OUT_DMAJOR) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(bh) * kD * p.s_q;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) out[static_cast<size_t>(ch * 32 + i) * p.s_q + grow] = __float2bfloat16_rn(v[i] * inv);
+      } else {
+        uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + rowidx * kD + ch * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint4 w;
+          w.x = pack_bf16x2(v[8 * i] * inv, v[8 * i + 1] * inv);
+          w.y = pack_bf16x2(v[8 * i + 2] * inv, v[8 * i + 3] * inv);
+          w.z = pack_bf16x2(v[8 * i + 4] * inv, v[8 * i + 5] * inv);
+          w.w = pack_bf16x2(v[8 * i + 6] * inv, v[8 * i + 7] * inv);
+          out[i] = w;
+        }
+      }
+    }
+    if (row_ok) {
+      if (!final_pass) {
+        p.acc_l[rowidx] = l;
+      } else if (p.flags & VOMNI_CM_LSE) {
+        const int groups = (p.s_q + 127) / 128;
+        p.lse[(static_cast<size_t>(bh) * 128 + (grow & 127)) * groups + (grow >> 7)] = c + logf(fmaxf(l, 1e-37f));
+      }
+    }
+  }
 }
 
 template <int kPoly, bool kSplit>
@@ -305,111 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
-    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
-    const int row = quad * 32 + lane;
-    const int grow = q0 + t * kTile + row;
-    const bool row_ok = grow < p.s_q;
-    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t col_s = tbase + lane_addr + kColS + t * 128;
-    const uint32_t col_o = tbase + lane_addr + kColO + t * 128;
-    const size_t rowidx = static_cast<size_t>(bh) * p.s_q + grow;
-    float c = 0.f;
-    if (row_ok) {
-      // c_i = scale * sqrt(kmax2 * ||q_i||^2), held in bf16 like the reference's c_row
-      // (ring_attention_const_max_fwd.py:585-591).
-      const float c32 = p.scale * sqrtf(p.kmax2[bh] * p.qn2[rowidx]);
-      c = __bfloat162float(__float2bfloat16_rn(c32));
-    }
-    const float neg_c2 = -c * 1.4426950408889634f;
-    // One thread of the last tile's warpgroup frees the K/V stages: S_{last}(j) complete means
-    // every QK of step j (and, issued before it, every PV of step j-1) has finished reading them.
-    const bool releaser = (t == kQT - 1) && row == 0;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    bool ok = true;
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      const int valid = p.n_keys - j * kTile;  // keys of this tile inside the pass's range
-      if (kSplit) {
-        if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
-        tc_fence_after();
-        if (releaser) release_stages(bars, j);
-        if (valid >= kTile)
-          softmax_tile_split<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t]);
-        else
-          softmax_tile_split<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t]);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&bars[P_FULL + 2 * t + 1]);
-      } else {
-        if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
-        tc_fence_after();
-        if (releaser) release_stages(bars, j);
-        if (valid >= kTile)
-          softmax_tile<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc);
-        else
-          softmax_tile<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&bars[P_FULL + 2 * t]);
-      }
-    }
-    const float rowsum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-    // ---------------------------------------------------------- epilogue
-    if (ok && mbar_wait(&bars[O_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) {
-      tc_fence_after();
-      const bool acc_in = p.flags & VOMNI_CM_ACC_IN;
-      const bool final_pass = p.flags & VOMNI_CM_FINAL;
-      float l = rowsum;
-      if (acc_in && row_ok) l += p.acc_l[rowidx];
-      const float inv = 1.f / fmaxf(l, 1e-37f);
-      float* acc_row = p.acc_o ? p.acc_o + rowidx * kD : nullptr;
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t o[32];
-        tmem_ld32(col_o + ch * 32, o);
-        tmem_ld_wait(o);
-        if (!row_ok) continue;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]);
-        if (acc_in) {
-          const float4* src = reinterpret_cast<const float4*>(acc_row + ch * 32);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 a = src[i];
-            v[4 * i] += a.x; v[4 * i + 1] += a.y; v[4 * i + 2] += a.z; v[4 * i + 3] += a.w;
-          }
-        }
-        if (!final_pass) {
-          float4* dst = reinterpret_cast<float4*>(acc_row + ch * 32);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        } else if (p.flags & VOMNI_CM_OUT_DMAJOR) {
-          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(bh) * kD * p.s_q;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) out[static_cast<size_t>(ch * 32 + i) * p.s_q + grow] = __float2bfloat16_rn(v[i] * inv);
-        } else {
-          uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + rowidx * kD + ch * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 w;
-            w.x = pack_bf16x2(v[8 * i] * inv, v[8 * i + 1] * inv);
-            w.y = pack_bf16x2(v[8 * i + 2] * inv, v[8 * i + 3] * inv);
-            w.z = pack_bf16x2(v[8 * i + 4] * inv, v[8 * i + 5] * inv);
-            w.w = pack_bf16x2(v[8 * i + 6] * inv, v[8 * i + 7] * inv);
-            out[i] = w;
-          }
-        }
-      }
-      if (row_ok) {
-        if (!final_pass) {
-          p.acc_l[rowidx] = l;
-        } else if (p.flags & VOMNI_CM_LSE) {
-          const int groups = (p.s_q + 127) / 128;
-          p.lse[(static_cast<size_t>(bh) * 128 + (grow & 127)) * groups + (grow >> 7)] = c + logf(fmaxf(l, 1e-37f));
-        }
-      }
-    }
+    softmax_role<kPoly, kSplit, false>(p, bars, abort_flag, tbase, warp, lane, q0, kTile, bh, n_tiles, 0u);
   }
 
   tc_fence_before();
@@ -417,6 +440,170 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);
+  }
+}
+
+// ---------------------------------------------------------------- CTA-pair attention
+// The same algorithm on a cluster of two CTAs (two SMs) sharing each MMA (tcgen05 cta_group::2):
+// a pair covers 2 x 256 query rows of one (batch, head); query tile t of the pair is 256 rows, 128
+// in each CTA's shared memory and TMEM. For QK the pair's 128-key K tile is split by key (64 keys
+// in each CTA); for PV the V tile is split by head dimension (64 columns in each CTA). Each CTA
+// therefore streams half the K/V bytes through its shared memory per MMA, which lifts the
+// shared-memory bandwidth limit of the one-CTA QK MMA (A 4 KB + B 4 KB per 64 cycles).
+// The even CTA issues every MMA; both CTAs run producers and softmax warpgroups. Operand loads
+// complete on the leader's barriers (cta_group::2 tile loads, no multicast), MMA completion is
+// committed to both CTAs, and the peer's softmax warps arrive on the leader's P barriers.
+constexpr uint32_t kPairKBytes = 64 * kD * 2;   // 16 KB: 64 keys x 128 dims
+constexpr uint32_t kPairVBytes = kTile * 64 * 2;  // 16 KB: 128 keys x 64 dims
+constexpr uint32_t kPairSmemQ = 0;
+constexpr uint32_t kPairSmemK = kPairSmemQ + kQT * kTileBytes;
+constexpr uint32_t kPairSmemV = kPairSmemK + 2 * kPairKBytes;
+constexpr uint32_t kPairSmemBar = kPairSmemV + 2 * kPairVBytes;
+constexpr uint32_t kPairSmemBytes = kPairSmemBar + 256 + 1024;
+constexpr uint32_t kIdescQKPair = idesc_bf16(256, 128, false);
+constexpr uint32_t kIdescPVPair = idesc_bf16(256, 128, true);
+
+__device__ __forceinline__ void issue_qk_pair(uint32_t d_s, uint64_t q_desc, uint64_t k_desc) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint64_t offa = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+    const uint64_t offb = ((kk >> 2) * (kPairKBytes / 2) + (kk & 3) * 32) >> 4;
+    mma_f16_ss_pair(d_s, q_desc + offa, k_desc + offb, kIdescQKPair, kk > 0);
+  }
+}
+__device__ __forceinline__ void issue_pv_pair_half(uint32_t d_o, uint32_t p_tmem, uint64_t v_desc, int hf, bool accumulate) {
+#pragma unroll
+  for (int k2 = 0; k2 < 4; ++k2) {
+    const int kk = hf * 4 + k2;
+    mma_f16_ts_pair(d_o, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPVPair, (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+template <int kPoly>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    cm_attend_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairSmemBar);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + kPairSmemBar + NBAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kPairSmemBar + NBAR * 8 + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int q_base = (blockIdx.x >> 1) * (2 * kTile * kQT) + static_cast<int>(rank) * kTile;  // this CTA's tile-0 rows
+  const int bh = blockIdx.y;
+  const int b = bh / p.heads;
+  const int h = bh % p.heads;
+  const int n_tiles = (p.n_keys + kTile - 1) / kTile;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[Q_FULL], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[K_FULL + i], 1);
+      mbar_init(&bars[K_EMPTY + i], 1);
+      mbar_init(&bars[V_FULL + i], 1);
+      mbar_init(&bars[V_EMPTY + i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&bars[S_FULL + i], 1);
+      mbar_init(&bars[P_FULL + i], 8);  // one arrival per softmax warp of both CTAs
+    }
+    mbar_init(&bars[O_FULL], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tbase = *tmem_base_slot;
+  const uint32_t lead_bars = mapa_shared(smem_u32(bars), 0);  // the leader's barrier array
+
+  uint8_t* sQ = smem + kPairSmemQ;
+  uint8_t* sK = smem + kPairSmemK;
+  uint8_t* sV = smem + kPairSmemV;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int x0 = h * kD;
+      if (leader) mbar_expect_tx(&bars[Q_FULL], 2 * kQT * kTileBytes);
+      for (int t = 0; t < kQT; ++t) {
+        const int qr = q_base + t * 2 * kTile;
+        tma_load_3d_pair(&tmQ, lead_bars + Q_FULL * 8, sQ + t * kTileBytes, x0, qr, b);
+        tma_load_3d_pair(&tmQ, lead_bars + Q_FULL * 8, sQ + t * kTileBytes + kHalfBytes, x0 + 64, qr, b);
+      }
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int k_row = p.k_start + j * kTile;
+        if (j >= 2 && !mbar_wait(&bars[K_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) break;
+        if (leader) mbar_expect_tx(&bars[K_FULL + st], 2 * kPairKBytes);
+        tma_load_3d_pair(&tmK, lead_bars + (K_FULL + st) * 8, sK + st * kPairKBytes, x0, k_row + rank * 64, b);
+        tma_load_3d_pair(&tmK, lead_bars + (K_FULL + st) * 8, sK + st * kPairKBytes + kPairKBytes / 2, x0 + 64,
+                         k_row + rank * 64, b);
+        if (j >= 2 && !mbar_wait(&bars[V_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x22)) break;
+        if (leader) mbar_expect_tx(&bars[V_FULL + st], 2 * kPairVBytes);
+        tma_load_3d_pair(&tmV, lead_bars + (V_FULL + st) * 8, sV + st * kPairVBytes, x0 + rank * 64, k_row, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      const uint64_t q_desc = make_sdesc(smem_u32(sQ), 16, 1024, kLayoutSW128);
+      const uint64_t k_desc = make_sdesc(smem_u32(sK), 16, 1024, kLayoutSW128);
+      const uint64_t v_desc = make_sdesc(smem_u32(sV), kPairVBytes, 1024, kLayoutSW128);
+      constexpr uint64_t kTileDesc = kTileBytes >> 4;
+      bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x23) &&
+                mbar_wait(&bars[K_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < kQT; ++t) {
+          issue_qk_pair(tbase + kColS + t * 128, q_desc + t * kTileDesc, k_desc);
+          tc_commit_pair(&bars[S_FULL + 2 * t]);
+        }
+      }
+      for (int j = 1; ok && j <= n_tiles; ++j) {
+        const int jj = j - 1;
+        const int vs = jj & 1, ks = j & 1;
+        for (int t = 0; t < kQT && ok; ++t) {
+          const uint32_t d_o = tbase + kColO + t * 128, d_s = tbase + kColS + t * 128;
+          for (int hf = 0; hf < 2 && ok; ++hf) {
+            if (!mbar_wait(&bars[P_FULL + 2 * t + hf], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
+            if (t == 0 && hf == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x26)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv_pair_half(d_o, d_s, v_desc + ((vs * kPairVBytes) >> 4), hf, jj > 0);
+          }
+          if (!ok) break;
+          if (j < n_tiles) {
+            if (t == 0 && !mbar_wait(&bars[K_FULL + ks], (j >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk_pair(d_s, q_desc + t * kTileDesc, k_desc + ((ks * kPairKBytes) >> 4));
+            tc_commit_pair(&bars[S_FULL + 2 * t]);
+          }
+        }
+      }
+      tc_commit_pair(&bars[O_FULL]);
+    }
+  } else {
+    softmax_role<kPoly, true, true>(p, bars, abort_flag, tbase, warp, lane, q_base, 2 * kTile, bh, n_tiles,
+                                    lead_bars + P_FULL * 8);
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its pair may still touch its barriers or TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 512);
   }
 }
 
@@ -559,13 +746,28 @@ extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void*
   p.status = device_status_ptr();
 
   // Tuning knobs (read once): VOMNI_CM_POLY = share of exponentials on the FMA pipe as 1/N
-  // (0 = none), VOMNI_CM_SPLIT = 1 to publish P in two key halves, 0 for whole tiles.
-  static int poly = -1, split = -1;
+  // (0 = none), VOMNI_CM_SPLIT = 1 to publish P in two key halves, 0 for whole tiles,
+  // VOMNI_CM_PAIR = 1 for the CTA-pair kernel.
+  static int poly = -1, split = -1, pair = -1;
   if (poly < 0) {
     const char* e = getenv("VOMNI_CM_POLY");
     poly = e ? atoi(e) : 0;
     const char* f = getenv("VOMNI_CM_SPLIT");
     split = f ? atoi(f) : 1;
+    const char* g = getenv("VOMNI_CM_PAIR");
+    pair = g ? atoi(g) : 1;
+  }
+  if (pair) {
+    CUtensorMap tk2;
+    rc = make_tmap_3d_bf16(&tk2, k, row_elems, s_kv, b, 64, 64, static_cast<uint64_t>(kv_stride));
+    if (rc) return rc;
+    auto pk = poly == 8 ? cm::cm_attend_pair_kernel<8> : cm::cm_attend_pair_kernel<0>;
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kPairSmemBytes));
+    const int pairs = (s_q + 4 * cm::kTile - 1) / (4 * cm::kTile);
+    dim3 grid(2 * pairs, b * h);
+    pk<<<grid, cm::kThreads, cm::kPairSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk2, tv, p);
+    VOMNI_CUDA_TRY(cudaGetLastError());
+    return VOMNI_OK;
   }
   auto kern = cm::cm_attend_kernel<0, false>;
   if (poly == 2) kern = split ? cm::cm_attend_kernel<2, true> : cm::cm_attend_kernel<2, false>;
