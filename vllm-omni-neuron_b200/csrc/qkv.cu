@@ -23,6 +23,8 @@
 #include "common.cuh"
 #include "host_util.h"
 
+#include <cstdlib>
+
 namespace vomni {
 namespace qkv {
 
@@ -220,6 +222,213 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, 2 * kBN);
+  }
+}
+
+// ---------------------------------------------------------------- ROW mode on CTA pairs
+// The same GEMM on a cluster of two CTAs sharing each MMA (tcgen05 cta_group::2, M=256): a pair
+// tile is 256 rows x 256 columns; each CTA loads its 128 rows of A and its 128 rows (half the
+// columns) of W per 128-byte k-block (32 KB per stage instead of 48 KB per 128 x 256 tile), so six
+// stages fit and W crosses each SM's shared memory half as often. Pair tiles are walked in groups
+// of kGroup row bands so the pairs in flight share both A bands and W column blocks in L2.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairABytes = kBM * kBK;  // 16 KB
+constexpr uint32_t kPairBBytes = 128 * kBK;  // 16 KB: this CTA's half of the 256 columns
+constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr uint32_t kPairSmemBar = kPairStages * kPairStageBytes;
+constexpr uint32_t kPairSmemBytes = kPairSmemBar + 256 + 1024;
+constexpr uint32_t kPairIdesc = idesc_e4m3(256, kBN);
+constexpr int kGroup = 8;
+
+struct PairTile {
+  int mb, nb;
+};
+// Pair-tile t -> (row band of 256, column block of 256): column-major inside groups of kGroup bands.
+VOMNI_DEV PairTile pair_tile(int t, int m_bands, int n_tiles) {
+  const int per_group = kGroup * n_tiles;
+  const int g = t / per_group;
+  const int r = t - g * per_group;
+  const int rows = min(kGroup, m_bands - g * kGroup);
+  return PairTile{g * kGroup + r % rows, r / rows};
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    qkv_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairSmemBar);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* acc_full = empty + kPairStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2], in the leader: one arrival per epilogue warp of the pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int nk = p.H / kBK;
+  const int m_bands = (p.T + 255) / 256;
+  const int n_all = m_bands * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPairStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * kBN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
+  const uint32_t lead_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < n_all; tile += n_pairs) {
+        const PairTile pt = pair_tile(tile, m_bands, p.n_tiles);
+        const int m0 = pt.mb * 256 + static_cast<int>(rank) * kBM;
+        const int n0 = pt.nb * kBN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kPairStages;
+          const uint32_t ph = (it / kPairStages) & 1;
+          if (it >= kPairStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x51)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * kPairStageBytes;
+          if (leader) mbar_expect_tx(&full[st], 2 * kPairStageBytes);
+          tma_load_2d_pair(&tmA, lead_full + st * 8, sa, kb * kBK, m0);
+          tma_load_2d_pair(&tmB, lead_full + st * 8, sa + kPairABytes, kb * kBK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < n_all; tile += n_pairs, ++lt) {
+        const int acc = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[acc], ((lt >> 1) & 1) ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x54)) break;
+        tc_fence_after();
+        const uint32_t tacc = tbase + acc * kBN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kPairStages;
+          const uint32_t ph = (it / kPairStages) & 1;
+          if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x52)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad0 = a_desc0 + ((st * kPairStageBytes) >> 4);
+          const uint64_t bd0 = ad0 + (kPairABytes >> 4);
+#pragma unroll
+          for (int k4 = 0; k4 < kBK / 32; ++k4)
+            mma_f8_ss_pair(tacc, ad0 + k4 * 2, bd0 + k4 * 2, kPairIdesc, (kb > 0 || k4 > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[st]);
+        }
+        if (ok) tc_commit_pair(&acc_full[acc]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    int lt = 0;
+    for (int tile = pair; tile < n_all; tile += n_pairs, ++lt) {
+      const int acc = lt & 1;
+      if (!mbar_wait(&acc_full[acc], (lt >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x53)) break;
+      tc_fence_after();
+      const PairTile pt = pair_tile(tile, m_bands, p.n_tiles);
+      const int nt = pt.nb;
+      const int n0 = nt * kBN;
+      const int grow = pt.mb * 256 + static_cast<int>(rank) * kBM + row;
+      const bool row_ok = grow < p.T;
+      const uint32_t tacc = tbase + lane_addr + acc * kBN;
+      const float rs = row_ok ? p.row_scale[grow] : 0.f;
+      float ss = 0.f, ss_lo = 0.f;
+      __nv_bfloat16* yrow = p.y + static_cast<size_t>(grow) * p.I + n0;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tacc + c * 32, r);
+        tmem_ld_wait(r);
+        const int col0 = n0 + c * 32;
+        const float4* cs4 = reinterpret_cast<const float4*>(p.chan_scale + col0);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 cs = cs4[i];
+          v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) * rs * cs.x;
+          v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) * rs * cs.y;
+          v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * rs * cs.z;
+          v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * rs * cs.w;
+        }
+        if (p.bias) {
+          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 bb = b4[i];
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(b2[j]);
+              v[8 * i + 2 * j] += f.x;
+              v[8 * i + 2 * j + 1] += f.y;
+            }
+          }
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
+          ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+        }
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(yrow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+        if (c == 3) {
+          ss_lo = ss;
+          ss = 0.f;
+        }
+      }
+      // This warp's rows of the accumulator have been read: tell the leader's MMA warp.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_acc_empty + acc * 8);
+      if (row_ok && p.sumsq && 2 * nt < p.n_norm_heads) {
+        float* dst = p.sumsq + static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt;
+        dst[0] = ss_lo;
+        dst[1] = ss;
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 2 * kBN);
   }
 }
 
@@ -593,10 +802,24 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
   p.m_tiles = (t + qkv::kBM - 1) / qkv::kBM;
   p.n_tiles = i / qkv::kBN;
   p.status = device_status_ptr();
-  static bool attr = false;
-  if (!attr) {
+  static int use_pair = -1;
+  if (use_pair < 0) {
+    const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
+    use_pair = e ? atoi(e) : 1;
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kSmemBytes));
-    attr = true;
+    VOMNI_CUDA_TRY(
+        cudaFuncSetAttribute(qkv::qkv_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kPairSmemBytes));
+  }
+  if (use_pair) {
+    CUtensorMap tb2;
+    rc = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
+    if (rc) return rc;
+    const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
+    const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
+    qkv::qkv_gemm_pair_kernel<<<2 * pairs, qkv::kThreads, qkv::kPairSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+        ta, tb2, p);
+    VOMNI_CUDA_TRY(cudaGetLastError());
+    return VOMNI_OK;
   }
   const int n_all = p.m_tiles * p.n_tiles;
   const int grid = n_all < num_sms() ? n_all : num_sms();
