@@ -38,6 +38,7 @@ CONFIGS = {
     "c2": dict(S=32760, latent=(21, 60, 104), desc="C2: Wan2.2-A14B 480x832x81 self-attention, S=32760 (21x30x52 tokens), H=40 D=128"),
     "c3": dict(S=32760, latent=None, desc="C3: fused adaLN (LayerNorm eps 1e-6, shift/scale) + FP8 row quant + FP8 QKV projection, T=32760 H=5120 I=15360"),
     "c4": dict(S=75600, latent=(21, 90, 160), desc="C4: Wan2.2-A14B 720x1280x81 self-attention, S=75600 (21x45x80 tokens), H=40 D=128"),
+    "oproj": dict(S=32760, latent=None, desc="Output projection of one C2 self-attention layer (d-major [1,40,128,32760] @ [5120,5120] + bias) with the norm2 gated residual and adaLN (LayerNorm + FP8 row quant)"),
 }
 METRIC = "ring-attn TFLOP/s at S=32760 (one Wan2.2-A14B self-attention layer), CP=N"
 
@@ -193,7 +194,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=list(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tokens", type=int, default=0, help="C3 only: override T (small case for profiling)")
+    ap.add_argument("--tokens", type=int, default=0, help="c3 / oproj: override the token count (small case for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -209,6 +210,8 @@ def main():
         return run_reference(args, world, rank, cfg, flops_layer, emit)
     if args.config == "c3":
         return run_c3(args, emit)
+    if args.config == "oproj":
+        return run_oproj(args, emit)
 
     import torch
     import torch.distributed as dist
@@ -535,6 +538,83 @@ def run_c3(args, emit):
         "gpu_launches": 6 * n,
     }
     emit(res)
+
+
+def run_oproj(args, emit):
+    """The step after the self-attention: o-projection of the d-major attention output with the gated
+    residual fused into its epilogue, then norm2 (adaLN LayerNorm + FP8 row quant), against the
+    unfused order (plain projection, then adaLN with its own residual step)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module(PKG)
+    pkg.build()
+    lib = importlib.import_module(PKG + "._lib")
+    S, K, H = (args.tokens or 32760), HIDDEN, HIDDEN
+    g = torch.Generator(device=dev).manual_seed(0)
+    active = torch.randn(1, HEADS, HEAD_DIM, S, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(K, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(H, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    res = torch.randn(1, S, H, generator=g, device=dev).to(torch.bfloat16)
+    gate = torch.randn(1, 1, H, generator=g, device=dev) * 0.3
+    n2w = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    n2b = (0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def proj():
+        return pkg.wan_o_proj(active, w, bias)
+
+    def fused():
+        return pkg.o_proj_gated_residual(active, w, bias, res, gate)
+
+    def fused_norm2():
+        return pkg.attn_out_norm2(active, w, bias, res, gate, n2w, n2b, eps=1e-6, quant="row")
+
+    def unfused_norm2():
+        y = pkg.wan_o_proj(active, w, bias)
+        return pkg.adaln_modulate(y, n2w, n2b, eps=1e-6, quant="row", residual=res, gate=gate)
+
+    def timeit(fn, n):
+        ts = []
+        for _ in range(n):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    for fn in (proj, fused, fused_norm2, unfused_norm2):
+        for _ in range(args.warmup):
+            fn()
+    torch.cuda.synchronize()
+    n = max(args.steps, 5)
+    sampler = ClockSampler(0)
+    sampler.start()
+    t_p, t_f, t_fn, t_un = timeit(proj, n), timeit(fused, n), timeit(fused_norm2, n), timeit(unfused_norm2, n)
+    clocks = sampler.stop()
+    assert lib.device_status() == 0
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    flops = 2.0 * S * K * H
+    emit({
+        "metric": "o-projection + norm2 after one C2 self-attention layer (ms per call)",
+        "value": round(t_fn, 4), "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": n,
+        "warmup": args.warmup, "dtype": "bf16 GEMM (fp32 accumulate), fp8 e4m3 row quant out", "data": "synthetic",
+        "config": {"workload": CONFIGS["oproj"]["desc"], "S": S, "K": K, "H": H, "l2": "flushed (256 MB write) before each call"},
+        "kernels": {
+            "oproj_gemm": {"ms": round(t_p, 4), "flops": flops, "TFLOP/s": round(flops / t_p / 1e9, 1),
+                           "frac_of_measured_bf16_burst": round(flops / t_p / 1e9 / bf16, 4)},
+            "oproj_gemm_gated_residual": {"ms": round(t_f, 4), "TFLOP/s": round(flops / t_f / 1e9, 1)},
+            "fused_step": {"ms": round(t_fn, 4), "kernels": "oproj_pair_kernel (residual epilogue) + adaln_kernel"},
+            "unfused_step": {"ms": round(t_un, 4), "kernels": "oproj_pair_kernel + adaln_kernel (residual step)"},
+        },
+        "clocks": clocks,
+        "gpu_launches": 5 * n,
+    })
 
 
 def run_reference(args, world, rank, cfg, flops_layer, emit):

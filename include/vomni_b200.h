@@ -169,6 +169,17 @@ VOMNI_API int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed, 
 /* [t, h + 4] packed rows (adaln ROW output) -> codes [t, h] + scales [t]. */
 VOMNI_API int vomni_qkv_unpack_rows(const void* packed, int t, int h, void* codes, float* scales, vomni_stream_t stream);
 
+/* ------------------------------------------------------------------ output projection
+ * _wan_o_proj (diffusion/models/wan2_2/wan2_2_transformer.py:246-254) on the d-major attention output
+ * attn [b, k, s] bf16 (k = heads*128; s % 8 == 0) and w [k, h] bf16 (h % 256 == 0, k % 64 == 0):
+ * y = bf16(bf16(x @ w) + bias) with x[t] = attn[:, :, t], written to out [b, s, h]. With a residual
+ * [b, s, h] bf16 the kernel writes the norm2 gated residual t = bf16(residual + gate * y) instead
+ * (gate fp32 [b, h] when gate_per_batch, else [h]; NULL = 1), the residual step of
+ * adaln_modulate(..., residual=, gate=) (wan2_2_transformer.py:1470-1489). */
+VOMNI_API int vomni_oproj_gemm(const void* attn, int b, int k, int s, const void* w, const void* bias, int h,
+                               const void* residual, const float* gate, int gate_per_batch, void* out,
+                               vomni_stream_t stream);
+
 /* ------------------------------------------------------------------ context-parallel ring
  * Replaces the ring driver of ring_attention_const_max_fwd(num_workers = N > 1)
  * (ring_attention_const_max_fwd.py:1196-1205 all_reduce(max) of the key norm, :1287-1398 K/V

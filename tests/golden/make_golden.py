@@ -12,7 +12,8 @@ cannot run without a Trainium toolchain):
   adaln_quant_torch.py), loaded by file path;
 * ``_eager_adaln`` (diffusion/quantization/adaln_kernels.py:51-84), loaded by file path;
 * ``WanRotaryPosEmbed`` / ``apply_rotary_emb_wan`` (diffusion/layers/rope.py), by file path;
-* ``_torch_attend`` (diffusion/models/wan2_2/wan2_2_transformer.py:640-650),
+* ``_torch_attend`` (diffusion/models/wan2_2/wan2_2_transformer.py:640-650) and ``_wan_o_proj``
+  (:246-254, its torch path: the NKI kernel's capability check is stubbed to False),
   ``DistributedRMSNorm`` (:855-893), ``_rope_rotate_half_caches``
   (diffusion/quantization/row_mx_modules.py:51-76) and the de-interleave loaders
   (diffusion/quantization/row_mx_loaders.py:26-71): their modules import the Neuron SDK at
@@ -173,14 +174,34 @@ def gen_rope_norm(rng: torch.Generator):
     )
 
 
+def gen_oproj():
+    wt = REF / "diffusion/models/wan2_2/wan2_2_transformer.py"
+    fns = _extract(wt, ["_wan_o_proj"], {"torch": torch, "_can_use_wan_o_proj_kernel": lambda *a: False})
+    rng = torch.Generator().manual_seed(20261202)
+    out = {}
+    for tag, (B, N, S, H) in {"a": (1, 2, 96, 256), "b": (2, 1, 40, 512)}.items():
+        active = torch.randn(B, N, 128, S, generator=rng).to(torch.bfloat16)  # d-major attention output
+        w = (0.02 * torch.randn(N * 128, H, generator=rng)).to(torch.bfloat16)
+        bias = (0.5 * torch.randn(1, H, generator=rng)).to(torch.bfloat16)
+        y = fns["_wan_o_proj"](active, w, bias)
+        out.update({f"{tag}|active": _bf16(active), f"{tag}|w": _bf16(w), f"{tag}|bias": _bf16(bias), f"{tag}|y": _bf16(y)})
+    np.savez_compressed(OUT / "wan_o_proj.npz", **out)
+
+
 def main():
     if not REF.exists():
         sys.exit(f"reference checkout not found at {REF}")
+    only = sys.argv[1:]
+    if only:  # regenerate only the named fixtures, e.g. ``make_golden.py oproj``
+        for name in only:
+            globals()[f"gen_{name}"]()
+        return
     rng = torch.Generator().manual_seed(20261201)
     gen_adaln(rng)
     gen_eager_adaln(rng)
     gen_attention(rng)
     gen_rope_norm(rng)
+    gen_oproj()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -141,3 +141,17 @@ def test_rotate_half_equals_interleaved_rope(golden):
     lo, hi = xd[..., :64], xd[..., 64:]
     out = np.concatenate([lo * c[..., :64] - hi * s[..., :64], hi * c[..., 64:] + lo * s[..., 64:]], axis=-1)
     np.testing.assert_array_equal(bf16_round(out), ref)
+
+
+def test_oproj_oracle_vs_reference_golden(golden):
+    """The o-projection restatement reproduces ``_wan_o_proj``'s own outputs."""
+    from oracle import oproj as oop
+
+    g = golden("wan_o_proj.npz")
+    for tag in ("a", "b"):
+        y = oop.wan_o_proj_ref(g[f"{tag}|active"], g[f"{tag}|w"], g[f"{tag}|bias"])
+        ref = g[f"{tag}|y"]
+        # fp32 accumulation order differs from torch's CPU matmul: at most one bf16 step apart
+        step = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref), 2.0 ** -100))) - 7)
+        assert (np.abs(y - ref) <= step * 1.0001).all(), tag
+        assert (y == ref).mean() > 0.97, tag

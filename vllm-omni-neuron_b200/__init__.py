@@ -6,6 +6,8 @@ Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call AP
 * :func:`wan_cp_self_attention` — the Wan attention processor core
 * :func:`adaln_modulate` — fused gated-residual + (Layer|RMS)Norm + modulation + FP8 row quant
 * :func:`row_mx_qkv_proj` — FP8 QKV projection with across-heads RMS norm + rotate-half RoPE
+* :func:`wan_o_proj`, :func:`attn_out_norm2` — output projection of the d-major attention output,
+  with the block's gated residual + norm2 adaLN
 
 Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``) built by
 :func:`build`.
@@ -15,6 +17,7 @@ from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .build import build
 from .leaf import wan_self_attention_fp8
+from .oproj import attn_out_norm2, o_proj_gated_residual, wan_o_proj
 from .qkv import (
     mx32_qkv_proj,
     pack_mx_scales,
@@ -28,9 +31,11 @@ from .ring import destroy_rings
 __all__ = [
     "adaln_modulate",
     "attention_local",
+    "attn_out_norm2",
     "build",
     "destroy_rings",
     "mx32_qkv_proj",
+    "o_proj_gated_residual",
     "pack_mx_scales",
     "quantize_qkv_weight",
     "quantize_qkv_weight_mx32",
@@ -38,5 +43,6 @@ __all__ = [
     "ring_attention_const_max_fwd",
     "row_mx_qkv_proj",
     "wan_cp_self_attention",
+    "wan_o_proj",
     "wan_self_attention_fp8",
 ]

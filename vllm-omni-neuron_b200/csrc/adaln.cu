@@ -139,11 +139,14 @@ __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
           if (p.gate) {
             const float4* g = reinterpret_cast<const float4*>(p.gate + static_cast<size_t>(mrow) * H + c * 8);
             const float4 g0 = g[0], g1 = g[1];
-            x[i][0] *= g0.x; x[i][1] *= g0.y; x[i][2] *= g0.z; x[i][3] *= g0.w;
-            x[i][4] *= g1.x; x[i][5] *= g1.y; x[i][6] *= g1.z; x[i][7] *= g1.w;
+            x[i][0] = __fmul_rn(x[i][0], g0.x); x[i][1] = __fmul_rn(x[i][1], g0.y);
+            x[i][2] = __fmul_rn(x[i][2], g0.z); x[i][3] = __fmul_rn(x[i][3], g0.w);
+            x[i][4] = __fmul_rn(x[i][4], g1.x); x[i][5] = __fmul_rn(x[i][5], g1.y);
+            x[i][6] = __fmul_rn(x[i][6], g1.z); x[i][7] = __fmul_rn(x[i][7], g1.w);
           }
+          // product and sum rounded separately (no FMA contraction), as the reference computes them
 #pragma unroll
-          for (int j = 0; j < 8; ++j) x[i][j] = __bfloat162float(__float2bfloat16_rn(r[j] + x[i][j]));
+          for (int j = 0; j < 8; ++j) x[i][j] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(r[j], x[i][j])));
           reinterpret_cast<uint4*>(p.residual_out + base)[c] = pack8(x[i]);
         }
       }

@@ -315,6 +315,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major)
   return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
+// kind::f16 descriptor with either operand MN-major (A: bit 15, B: bit 16).
+__host__ __device__ constexpr uint32_t idesc_bf16_mn(int m, int n, bool a_mn_major, bool b_mn_major) {
+  return idesc_bf16(m, n, b_mn_major) | ((a_mn_major ? 1u : 0u) << 15);
+}
 // Instruction descriptor, kind::mxf8f6f4.block_scale: e4m3 A/B (K-major), UE8M0 scales (bit 23),
 // fp32 D, scale byte `sf_id` of each 32-bit scale word for both A (bits 29-30) and B (bits 4-5).
 __host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n, uint32_t sf_id) {

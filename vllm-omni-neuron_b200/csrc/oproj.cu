@@ -1,0 +1,287 @@
+// Output projection of the Wan self-attention with the block's norm2 gated residual fused in.
+//
+// Reference: _wan_o_proj (vllm_omni_neuron/diffusion/models/wan2_2/wan2_2_transformer.py:246-254):
+//   x = active.reshape(B, N*D, S).transpose(1, 2);  y = x @ W + b      (bf16 tensors, fp32 accumulate)
+// consumed by the block's norm2 (:1470-1489):
+//   hidden_states, norm_h = adaln_modulate(y, ..., residual=hidden_states, gate=gate_msa)
+// whose residual step is t = bf16(residual + gate * y) (fp32 product; adaln_kernels.py:51-84).
+// torch rounds the matmul to bf16 before the bias add, and the sum again: y = bf16(bf16(acc) + b).
+//
+// B200 kernel: the d-major attention output [B, N*D, S] is read in place as an MN-major A operand
+// (tokens contiguous) and W [N*D, H] as an MN-major B operand, both by TMA with 128-byte swizzle, so
+// neither the reference's transpose nor a weight repack is needed. CTA pairs share each
+// tcgen05.mma (cta_group::2, M=256 tokens, N=256 columns, K=16): each CTA stages its 128 tokens and
+// its 128 output columns per 64-deep k-block (32 KB per stage, six stages). The epilogue rounds as
+// torch does, adds the bias, and with a residual writes t = bf16(residual + gate * y) instead of y,
+// so norm2 reads t once (the adaLN kernel then runs without its residual step).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace vomni {
+namespace oproj {
+
+constexpr int kThreads = 192;
+constexpr int kStages = 6;
+constexpr int kBK = 64;                              // K rows per stage (bf16)
+constexpr uint32_t kChunkBytes = kBK * 128;          // 8 KB: 64 K rows x 64 contiguous elements
+constexpr uint32_t kABytes = 2 * kChunkBytes;        // this CTA's 128 tokens
+constexpr uint32_t kBBytes = 2 * kChunkBytes;        // this CTA's 128 output columns
+constexpr uint32_t kStageBytes = kABytes + kBBytes;  // 32 KB
+constexpr uint32_t kSmemBar = kStages * kStageBytes;
+constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;
+constexpr uint32_t kIdesc = idesc_bf16_mn(256, 256, true, true);
+constexpr int kGroup = 8;
+
+struct Params {
+  int B, S, K, H;
+  int m_bands;  // ceil(S / 256) per batch element
+  int n_tiles;  // H / 256
+  const __nv_bfloat16* bias;      // [H] or null
+  const __nv_bfloat16* residual;  // [B, S, H] or null
+  const float* gate;              // [B, H] or [H] (gate_per_batch = 0) or null
+  int gate_per_batch;
+  __nv_bfloat16* out;  // [B, S, H]
+  int* status;
+};
+
+struct Tile {
+  int b, mb, nb;
+};
+// Pair tile t -> (batch, 256-token band, 256-column block); column-major inside groups of kGroup
+// bands so the pairs in flight share A bands and W column blocks in L2.
+VOMNI_DEV Tile tile_of(int t, const Params& p) {
+  const int bands = p.B * p.m_bands;
+  const int per_group = kGroup * p.n_tiles;
+  const int g = t / per_group;
+  const int r = t - g * per_group;
+  const int rows = min(kGroup, bands - g * kGroup);
+  const int band = g * kGroup + r % rows;
+  return Tile{band / p.m_bands, band % p.m_bands, r / rows};
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    oproj_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmemBar);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2], in the leader: one arrival per epilogue warp of the pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int nk = p.K / kBK;
+  const int n_all = p.B * p.m_bands * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
+  const uint32_t lead_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < n_all; tile += n_pairs) {
+        const Tile tt = tile_of(tile, p);
+        const int tok0 = tt.mb * 256 + static_cast<int>(rank) * 128;
+        const int n0 = tt.nb * 256 + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (it >= kStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x61)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * kStageBytes;
+          const uint32_t bar = lead_full + st * 8;
+          if (leader) mbar_expect_tx(&full[st], 2 * kStageBytes);
+          tma_load_3d_pair(&tmA, bar, sa, tok0, kb * kBK, tt.b);
+          tma_load_3d_pair(&tmA, bar, sa + kChunkBytes, tok0 + 64, kb * kBK, tt.b);
+          tma_load_2d_pair(&tmB, bar, sa + kABytes, n0, kb * kBK);
+          tma_load_2d_pair(&tmB, bar, sa + kABytes + kChunkBytes, n0 + 64, kb * kBK);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      // MN-major SW128 operands: 64-element chunks kChunkBytes apart (LBO), 8-row K groups 1 KB
+      // apart (SBO); one K=16 step = 16 rows = +2 KB.
+      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), kChunkBytes, 1024, kLayoutSW128);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < n_all; tile += n_pairs, ++lt) {
+        const int acc = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[acc], ((lt >> 1) & 1) ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x64)) break;
+        tc_fence_after();
+        const uint32_t tacc = tbase + acc * 256;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x62)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad0 = a_desc0 + ((st * kStageBytes) >> 4);
+          const uint64_t bd0 = ad0 + (kABytes >> 4);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_f16_ss_pair(tacc, ad0 + ((k * 2048) >> 4), bd0 + ((k * 2048) >> 4), kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[st]);
+        }
+        if (ok) tc_commit_pair(&acc_full[acc]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    int lt = 0;
+    for (int tile = pair; tile < n_all; tile += n_pairs, ++lt) {
+      const int acc = lt & 1;
+      if (!mbar_wait(&acc_full[acc], (lt >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x63)) break;
+      tc_fence_after();
+      const Tile tt = tile_of(tile, p);
+      const int tok = tt.mb * 256 + static_cast<int>(rank) * 128 + row;
+      const bool row_ok = tok < p.S;
+      const int n0 = tt.nb * 256;
+      const size_t orow = (static_cast<size_t>(tt.b) * p.S + tok) * p.H;
+      const float* gate = p.gate ? p.gate + (p.gate_per_batch ? static_cast<size_t>(tt.b) * p.H : 0) : nullptr;
+      const uint32_t tacc = tbase + lane_addr + acc * 256;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tacc + c * 32, r);
+        tmem_ld_wait(r);
+        if (!row_ok) continue;
+        const int col0 = n0 + c * 32;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[i])));  // torch matmul out
+        if (p.bias) {
+          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 bb = b4[i];
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(b2[j]);
+              v[8 * i + 2 * j] = __bfloat162float(__float2bfloat16_rn(v[8 * i + 2 * j] + f.x));
+              v[8 * i + 2 * j + 1] = __bfloat162float(__float2bfloat16_rn(v[8 * i + 2 * j + 1] + f.y));
+            }
+          }
+        }
+        if (p.residual) {
+          const uint4* r4 = reinterpret_cast<const uint4*>(p.residual + orow + col0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 rr = r4[i];
+            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(r2[j]);
+              const int e = 8 * i + 2 * j;
+              const float g0 = gate ? gate[col0 + e] : 1.f, g1 = gate ? gate[col0 + e + 1] : 1.f;
+              v[e] = __fadd_rn(f.x, __fmul_rn(v[e], g0));  // separate roundings, as the reference
+              v[e + 1] = __fadd_rn(f.y, __fmul_rn(v[e + 1], g1));
+            }
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(p.out + orow + col0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                              pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_acc_empty + acc * 8);
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 512);
+  }
+}
+
+}  // namespace oproj
+}  // namespace vomni
+
+using namespace vomni;
+
+extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const void* w, const void* bias, int h,
+                                const void* residual, const float* gate, int gate_per_batch, void* out,
+                                vomni_stream_t stream) {
+  if (!attn || !w || !out) return VOMNI_EINVAL;
+  if (gate && !residual) return VOMNI_EINVAL;
+  if (b <= 0 || s <= 0 || k <= 0 || h <= 0 || (k % oproj::kBK) || (h % 256)) return VOMNI_EBADSHAPE;
+  if ((s % 8) || b > 65535) return VOMNI_EBADSHAPE;  // token rows of the d-major input must be 16-byte pitched
+  const uintptr_t al = reinterpret_cast<uintptr_t>(attn) | reinterpret_cast<uintptr_t>(w) |
+                       reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(residual) |
+                       reinterpret_cast<uintptr_t>(out);
+  if (al & 15) return VOMNI_EALIGN;
+  int rc = require_sm100();
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  rc = make_tmap_3d_bf16(&ta, attn, static_cast<uint64_t>(s), static_cast<uint64_t>(k), static_cast<uint64_t>(b), 64, 64, 0);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, static_cast<uint64_t>(h), static_cast<uint64_t>(k),
+                    static_cast<uint64_t>(h) * 2, 64, 64);
+  if (rc) return rc;
+  oproj::Params p;
+  p.B = b;
+  p.S = s;
+  p.K = k;
+  p.H = h;
+  p.m_bands = (s + 255) / 256;
+  p.n_tiles = h / 256;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.gate = gate;
+  p.gate_per_batch = gate_per_batch ? 1 : 0;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.status = device_status_ptr();
+  static bool attr = false;
+  if (!attr) {
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(oproj::oproj_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, oproj::kSmemBytes));
+    attr = true;
+  }
+  const long long tiles = static_cast<long long>(b) * p.m_bands * p.n_tiles;
+  const int pairs = static_cast<int>(tiles < num_sms() / 2 ? tiles : num_sms() / 2);
+  oproj::oproj_pair_kernel<<<2 * pairs, oproj::kThreads, oproj::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
