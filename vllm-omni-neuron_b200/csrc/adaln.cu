@@ -16,6 +16,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include "common.cuh"
 #include "host_util.h"
 
 namespace vomni {
@@ -55,10 +56,11 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 // Block-wide reduction; `red` holds kWarps floats. Ends with every thread holding the result.
 template <bool kMax>
+// One __syncthreads per reduction: each reduction of a row writes its own slot of `red`, and
+// consecutive uses of one slot are always separated by another reduction's barrier.
 __device__ __forceinline__ float block_reduce(float v, float* red) {
   v = kMax ? warp_max(v) : warp_sum(v);
   const int w = threadIdx.x >> 5;
-  __syncthreads();
   if ((threadIdx.x & 31) == 0) red[w] = v;
   __syncthreads();
   float r = red[0];
@@ -93,48 +95,73 @@ __device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
   return r;
 }
 
+VOMNI_DEV void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+VOMNI_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+VOMNI_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // NV = 16-byte chunks (8 values) per thread; a row holds up to NV * 128 * 8 values.
-// Persistent: CTA c handles rows c, c + gridDim.x, ...; the next row's hidden (and residual) chunks
-// are loaded before the current row's reductions, and the modulation vectors stay in registers
+// Persistent: CTA c handles rows c, c + gridDim.x, ...; each thread streams its own chunks of the
+// next kS-1 rows (hidden, and residual) into a kS-slot shared-memory ring with cp.async, so
+// kS-1 rows per CTA are in flight while one is reduced; the modulation vectors stay in registers
 // for as long as consecutive rows share them.
-template <int NV, bool kRes>
-__global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
-  __shared__ float red[kWarps];
+template <int NV, bool kRes, int kS>
+__global__ void __launch_bounds__(kThreads, NV <= 6 ? 3 : 1) adaln_kernel(const Params p) {
+  extern __shared__ uint4 ring[];  // [kS][H/8] hidden, then [kS][H/8] residual
+  // Reduction slots, double-buffered by row parity: a row may take a single barrier, and a slot
+  // is rewritten only two rows later, after every thread has passed the next row's barrier.
+  __shared__ float red_sq[2][kWarps];       // LayerNorm sum / RMS sum of squares
+  __shared__ float red_stat_v[2][kWarps];   // LayerNorm squared deviations
+  __shared__ float red_max[2][kWarps];      // absmax for the row quant
+  int parity = 0;
   const int H = p.H;
   const int nchunk = H >> 3;
   long long row = blockIdx.x;
   if (row >= p.rows) return;
 
-  uint4 hn[NV], rn[NV];  // next row, raw bf16
-  auto load_row = [&](long long r) {
-    const uint4* hp = reinterpret_cast<const uint4*>(p.hidden + static_cast<size_t>(r) * H);
-    const uint4* rp = kRes ? reinterpret_cast<const uint4*>(p.residual + static_cast<size_t>(r) * H) : nullptr;
+  const long long G = gridDim.x;
+  auto issue = [&](long long r, int slot) {
+    if (r < p.rows) {
+      const uint4* hp = reinterpret_cast<const uint4*>(p.hidden + static_cast<size_t>(r) * H);
+      const uint4* rp = kRes ? reinterpret_cast<const uint4*>(p.residual + static_cast<size_t>(r) * H) : nullptr;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = threadIdx.x + i * kThreads;
-      if (c < nchunk) {
-        hn[i] = __ldcs(hp + c);  // streamed once: evict-first
-        if (kRes) rn[i] = __ldcs(rp + c);
+      for (int i = 0; i < NV; ++i) {
+        const int c = threadIdx.x + i * kThreads;
+        if (c < nchunk) {
+          cp_async16(ring + slot * nchunk + c, hp + c);
+          if (kRes) cp_async16(ring + (kS + slot) * nchunk + c, rp + c);
+        }
       }
     }
+    cp_async_commit();  // one group per row slot, empty past the end, so wait counts stay uniform
   };
-  load_row(row);
+#pragma unroll
+  for (int s0 = 0; s0 < kS - 1; ++s0) issue(row + s0 * G, s0);
+  int k = 0;
   long long cached_mrow = -1;
   uint4 mul_r[NV], add_r[NV];
   const uint4 one_bf16x8 = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
 
   while (row < p.rows) {
-    const long long next = row + gridDim.x;
+    const long long next = row + G;
     const size_t base = static_cast<size_t>(row) * H;
     const long long mrow = row / p.rows_per_mod;
+    issue(row + (kS - 1) * G, (k + kS - 1) % kS);  // refill the slot this thread finished with last row
+    cp_async_wait<kS - 1>();                        // groups complete in order: this row has landed
+    const int slot = k % kS;
     float x[NV][8];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      unpack8(hn[i], x[i]);
+      const int cc = threadIdx.x + i * kThreads;
+      if (cc < nchunk) unpack8(ring[slot * nchunk + cc], x[i]);
       if (kRes) {
-        const int c = threadIdx.x + i * kThreads;
+        const int c = cc;
         float r[8];
-        unpack8(rn[i], r);
+        if (c < nchunk) unpack8(ring[(kS + slot) * nchunk + c], r);
         if (c < nchunk) {
           if (p.gate) {
             const float4* g = reinterpret_cast<const float4*>(p.gate + static_cast<size_t>(mrow) * H + c * 8);
@@ -155,7 +182,6 @@ __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
         for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
       }
     }
-    if (next < p.rows) load_row(next);  // overlaps this row's reductions and stores
     if (mrow != cached_mrow) {
       cached_mrow = mrow;
 #pragma unroll
@@ -165,38 +191,38 @@ __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
         add_r[i] = (p.add && c < nchunk) ? reinterpret_cast<const uint4*>(p.add + static_cast<size_t>(mrow) * H)[c] : make_uint4(0, 0, 0, 0);
       }
     }
-    // ---- statistics (fp32, two-pass for LayerNorm)
+    // ---- statistics (fp32): per-thread two-pass mean / squared deviations, merged across the row
     const float invH = 1.f / static_cast<float>(H);
     float mean = 0.f, rstd = 1.f;
     if (p.norm == 0) {
-      float sm = 0.f;
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) sm += x[i][j];
-      mean = block_reduce<false>(sm, red) * invH;
-      float v = 0.f;
+        for (int j = 0; j < 8; ++j) sm[j & 3] += x[i][j];
+      mean = block_reduce<false>((sm[0] + sm[1]) + (sm[2] + sm[3]), red_sq[parity]) * invH;
+      float m2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
         if (threadIdx.x + i * kThreads < nchunk) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float d = x[i][j] - mean;
-            v = fmaf(d, d, v);
+            m2[j & 3] = fmaf(d, d, m2[j & 3]);
           }
         }
       }
-      rstd = rsqrtf(block_reduce<false>(v, red) * invH + p.eps);
+      rstd = rsqrtf(block_reduce<false>((m2[0] + m2[1]) + (m2[2] + m2[3]), red_stat_v[parity]) * invH + p.eps);
     } else if (p.norm == 1) {
-      float v = 0.f;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v = fmaf(x[i][j], x[i][j], v);
-      rstd = rsqrtf(block_reduce<false>(v, red) * invH + p.eps);
+        for (int j = 0; j < 8; ++j) v[j & 3] = fmaf(x[i][j], x[i][j], v[j & 3]);
+      rstd = rsqrtf(block_reduce<false>((v[0] + v[1]) + (v[2] + v[3]), red_sq[parity]) * invH + p.eps);
     }
     // ---- normalise + modulate (mul defaults to 1, add to 0)
-    float amax = 0.f;
+    float am[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       float m[8], a[8];
@@ -207,9 +233,10 @@ __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
         float y = p.norm == 2 ? x[i][j] : (x[i][j] - mean) * rstd;
         y = fmaf(y, m[j], a[j]);
         x[i][j] = y;
-        amax = fmaxf(amax, fabsf(y));
+        am[j & 3] = fmaxf(am[j & 3], fabsf(y));
       }
     }
+    float amax = fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3]));
     // ---- quantise + store
     if (p.quant == 0) {
 #pragma unroll
@@ -218,7 +245,7 @@ __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
         if (c < nchunk) __stcs(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base) + c, pack8(x[i]));
       }
     } else if (p.quant == 1) {
-      amax = block_reduce<true>(amax, red);
+      amax = block_reduce<true>(amax, red_max[parity]);
       const float scale = fmaxf(amax / p.fp8_range, 1e-6f);
       // codes = y * (1 / scale), the reciprocal-multiply of the reference kernel (adaln_quant.py:520-536)
       const float inv = __frcp_rn(scale);
@@ -272,22 +299,33 @@ __global__ void __launch_bounds__(kThreads) adaln_kernel(const Params p) {
       }
     }
     row = next;
+    parity ^= 1;
+    ++k;
   }
+  cp_async_wait<0>();  // no copy into shared memory may outlive the CTA
 }
 
-template <int NV>
-int launch(const Params& p, cudaStream_t st) {
-  // Persistent grid: as many CTAs as fit on the device at once, each walking rows with a one-row
-  // prefetch.
-  auto kern = p.residual ? adaln_kernel<NV, true> : adaln_kernel<NV, false>;
+template <int NV, int kS>
+int launch_s(const Params& p, cudaStream_t st) {
+  // Persistent grid: as many CTAs as fit on the device at once, each streaming rows through its ring.
+  auto kern = p.residual ? adaln_kernel<NV, true, kS> : adaln_kernel<NV, false, kS>;
+  const size_t smem = static_cast<size_t>(kS) * p.H * 2 * (p.residual ? 2 : 1);
+  VOMNI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   int per_sm = 0;
-  VOMNI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0));
+  VOMNI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
   if (per_sm < 1) per_sm = 1;
   const long long cap = static_cast<long long>(num_sms()) * per_sm;
   const unsigned grid = static_cast<unsigned>(p.rows < cap ? p.rows : cap);
-  kern<<<grid, kThreads, 0, st>>>(p);
+  kern<<<grid, kThreads, smem, st>>>(p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
+}
+
+// Four ring slots while they fit in 80 KB per CTA, else two.
+template <int NV>
+int launch(const Params& p, cudaStream_t st) {
+  const size_t row_bytes = static_cast<size_t>(p.H) * 2 * (p.residual ? 2 : 1);
+  return 4 * row_bytes <= 80 * 1024 ? launch_s<NV, 4>(p, st) : launch_s<NV, 2>(p, st);
 }
 
 }  // namespace adaln
