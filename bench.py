@@ -311,7 +311,7 @@ def main():
     if kern_ms:
         ach = kern_flops / (kern_ms / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s", "frac": round(ach / peak, 4),
-                "traffic": traffic, "kernel": "cm_attend_kernel", "kernel_ms": round(kern_ms, 4), "peak_source": peak_src}
+                "traffic": traffic, "kernel": "cm_attend_pair_kernel", "kernel_ms": round(kern_ms, 4), "peak_source": peak_src}
 
     # ---------------- exposed ring communication (N > 1): the same pass plan over local data only
     ring_info = None
@@ -388,7 +388,7 @@ def main():
         cpu = {"value": round(val, 5), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
                "sample": f"_torch_attend restated (oracle/attention.py torch_attend, numpy fp32): {heads_s} head x {rows_s} query rows x {S} keys, repeated {el:.1f}s ({fl/1e9:.0f} GFLOP)"}
 
-    launches_per_step = 2  # cm_norms_kernel + cm_attend_kernel
+    launches_per_step = 2  # cm_norms_kernel + cm_attend_pair_kernel
     if world > 1:
         ring = importlib.import_module(PKG + ".ring")
         launches_per_step = 1 + len(ring.phase_plan(world))  # prologue + one attention pass per ring pass
