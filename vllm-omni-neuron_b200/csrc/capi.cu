@@ -115,6 +115,20 @@ int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
   return r == CUDA_SUCCESS ? VOMNI_OK : VOMNI_ECUDA;
 }
 
+int make_tmap_2d_plain(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                       uint64_t pitch_bytes, uint32_t box0, uint32_t box1) {
+  int rc = get_encoder();
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch_bytes % 16)) return VOMNI_EALIGN;
+  cuuint64_t dims[2] = {dim0, dim1};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box0, box1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? VOMNI_OK : VOMNI_ECUDA;
+}
+
 }  // namespace vomni
 
 extern "C" int vomni_abi_version(void) { return 1; }

@@ -39,5 +39,8 @@ int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t dim0, uint64_
 // explicit row pitch in bytes, box {box0, box1}, 128-byte swizzle, OOB reads as zero.
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
                  uint64_t pitch_bytes, uint32_t box0, uint32_t box1);
+// Same without swizzle (plain row-major boxes), e.g. for 512-byte scale-factor atoms.
+int make_tmap_2d_plain(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                       uint64_t pitch_bytes, uint32_t box0, uint32_t box1);
 
 }  // namespace vomni

@@ -658,6 +658,191 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   }
 }
 
+// MX-32 on CTA pairs: 256 x 256 pair tiles, cta_group::2 block-scaled MMA (M=256, N=256, K=32).
+// Each CTA stages its 128 rows of X, its 128 rows of W, the scale atom of its X rows and the two
+// atoms of all 256 W rows (every SM applies the scales of the full N=256 to its 128 output rows);
+// the leader copies both CTAs' atoms into their TMEM with one tcgen05.cp.cta_group::2 per atom.
+constexpr int kMxPairStages = 6;
+constexpr uint32_t kMxPairABytes = kBM * kBK;  // 16 KB
+constexpr uint32_t kMxPairBBytes = 128 * kBK;  // 16 KB
+constexpr uint32_t kMxPairStageBytes =
+    (kMxPairABytes + kMxPairBBytes + kMxSfaBytes + kMxSfbBytes + 1023) / 1024 * 1024;  // 34 KB
+constexpr uint32_t kMxPairTx = kMxPairABytes + kMxPairBBytes + kMxSfaBytes + kMxSfbBytes;
+constexpr uint32_t kMxPairSmemBar = kMxPairStages * kMxPairStageBytes;
+constexpr uint32_t kMxPairSmemBytes = kMxPairSmemBar + 256 + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
+    qkv_gemm_mx_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            const __grid_constant__ CUtensorMap tmSfa, const __grid_constant__ CUtensorMap tmSfb,
+                            const MxParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kMxPairSmemBar);
+  uint64_t* empty = full + kMxPairStages;
+  uint64_t* acc_full = empty + kMxPairStages;
+  uint64_t* acc_empty = acc_full + 1;  // in the leader: one arrival per epilogue warp of the pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int nk = p.H / kBK;
+  const int m_bands = (p.T + 255) / 256;
+  const int n_all = m_bands * p.n_tiles;
+  const int n128 = p.I / 128;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kMxPairStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 16);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lead_full = mapa_shared(smem_u32(full), 0);
+  const uint32_t lead_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < n_all; tile += n_pairs) {
+        const PairTile pt = pair_tile(tile, m_bands, p.n_tiles);
+        const int mblk = pt.mb * 2 + static_cast<int>(rank);  // this CTA's 128-row block of X
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kMxPairStages;
+          const uint32_t ph = (it / kMxPairStages) & 1;
+          if (it >= kMxPairStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x71)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + st * kMxPairStageBytes;
+          const uint32_t bar = lead_full + st * 8;
+          if (leader) mbar_expect_tx(&full[st], 2 * kMxPairTx);
+          tma_load_2d_pair(&tmA, bar, sa, kb * kBK, mblk * kBM);
+          tma_load_2d_pair(&tmB, bar, sa + kMxPairABytes, kb * kBK, pt.nb * kBN + static_cast<int>(rank) * 128);
+          // scale atoms as rows of 128 bytes: [H/128][row blocks][4 rows of 128 B]
+          tma_load_2d_pair(&tmSfa, bar, sa + kMxPairABytes + kMxPairBBytes, 0, (kb * p.m_tiles + mblk) * 4);
+          tma_load_2d_pair(&tmSfb, bar, sa + kMxPairABytes + kMxPairBBytes + kMxSfaBytes, 0, (kb * n128 + pt.nb * 2) * 4);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128);
+      const uint64_t sf_desc0 = make_sdesc(smem_u32(smem + kMxPairABytes + kMxPairBBytes), 16, 128, 0);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < n_all; tile += n_pairs, ++lt) {
+        if (lt >= 1 && !mbar_wait(acc_empty, (lt - 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x74)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int st = it % kMxPairStages;
+          const uint32_t ph = (it / kMxPairStages) & 1;
+          if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x72)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t sdesc = sf_desc0 + ((st * kMxPairStageBytes) >> 4);
+          const uint32_t t_sfa = tbase + kMxColSf + st * 12;
+          const uint32_t t_sfb = t_sfa + 4;
+          tmem_cp_32x128b_warpx4_pair(t_sfa, sdesc);
+          tmem_cp_32x128b_warpx4_pair(t_sfb, sdesc + (kMxSfaBytes >> 4));
+          tmem_cp_32x128b_warpx4_pair(t_sfb + 4, sdesc + ((kMxSfaBytes + kSfAtomBytes) >> 4));
+          const uint64_t ad0 = a_desc0 + ((st * kMxPairStageBytes) >> 4);
+          const uint64_t bd0 = ad0 + (kMxPairABytes >> 4);
+#pragma unroll
+          for (int k4 = 0; k4 < kBK / 32; ++k4)
+            mma_mxf8_ss_pair(tbase, ad0 + k4 * 2, bd0 + k4 * 2, idesc_mxf8(256, kBN, k4), (kb > 0 || k4 > 0) ? 1u : 0u,
+                             t_sfa | (static_cast<uint32_t>(k4) << 30), t_sfb | (static_cast<uint32_t>(k4) << 30));
+          tc_commit_pair(&empty[st]);
+        }
+        if (ok) tc_commit_pair(acc_full);
+      }
+    }
+  } else {
+    // Eight epilogue warps per CTA (two per TMEM lane quadrant, 128 columns each): drain the
+    // accumulator to registers, release it to the leader's MMA warp, then store.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    int lt = 0;
+    for (int tile = pair; tile < n_all; tile += n_pairs, ++lt) {
+      if (!mbar_wait(acc_full, lt & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x73)) break;
+      tc_fence_after();
+      const PairTile pt = pair_tile(tile, m_bands, p.n_tiles);
+      const int nt = pt.nb;
+      const int n0 = nt * kBN + half * 128;
+      const int grow = pt.mb * 256 + static_cast<int>(rank) * kBM + row;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + lane_addr + half * 128 + c * 32, r);
+        tmem_ld_wait(r);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (p.bias) {
+          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 bb = b4[i];
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(b2[j]);
+              v[8 * i + 2 * j] += f.x;
+              v[8 * i + 2 * j + 1] += f.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
+        ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+      }
+      if (grow < p.T) {
+        uint4* dst = reinterpret_cast<uint4*>(p.y + static_cast<size_t>(grow) * p.I + n0);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+      if (p.sumsq && grow < p.T && 2 * nt + half < p.n_norm_heads)
+        p.sumsq[static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt + half] = ss;
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, 512);
+  }
+}
+
 // [T, H + 4] packed rows (codes then fp32 scale; rows only 4-byte aligned) -> codes [T, H] + scale [T].
 __global__ void unpack_rows_kernel(const uint8_t* __restrict__ packed, int T, int H, uint8_t* __restrict__ codes,
                                    float* __restrict__ scales) {
@@ -893,11 +1078,31 @@ extern "C" int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed,
   p.sumsq = sumsq;
   p.n_norm_heads = (q_dim + kv_dim) / 128;
   p.status = device_status_ptr();
-  static bool attr = false;
-  if (!attr) {
+  static int use_pair = -1;
+  if (use_pair < 0) {
+    const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
+    use_pair = e ? atoi(e) : 1;
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         qkv::kMxSmemBytes));
-    attr = true;
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        qkv::kMxPairSmemBytes));
+  }
+  if (use_pair) {
+    // X scale atoms must exist for every 128-row block a pair tile touches (pair bands are 256 rows)
+    CUtensorMap tb2, tsa, tsb;
+    rc = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
+    if (rc) return rc;
+    const uint64_t k128 = static_cast<uint64_t>(h / 128);
+    rc = make_tmap_2d_plain(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_sf_packed, 128, k128 * p.m_tiles * 4, 128, 128, 4);
+    if (rc) return rc;
+    rc = make_tmap_2d_plain(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_sf_packed, 128, k128 * (i / 128) * 4, 128, 128, 8);
+    if (rc) return rc;
+    const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
+    const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
+    qkv::qkv_gemm_mx_pair_kernel<<<2 * pairs, qkv::kMxThreads, qkv::kMxPairSmemBytes,
+                                   reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb2, tsa, tsb, p);
+    VOMNI_CUDA_TRY(cudaGetLastError());
+    return VOMNI_OK;
   }
   const int n_all = p.m_tiles * p.n_tiles;
   const int grid = n_all < num_sms() ? n_all : num_sms();
