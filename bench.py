@@ -38,6 +38,7 @@ CONFIGS = {
     "c2": dict(S=32760, latent=(21, 60, 104), desc="C2: Wan2.2-A14B 480x832x81 self-attention, S=32760 (21x30x52 tokens), H=40 D=128"),
     "c3": dict(S=32760, latent=None, desc="C3: fused adaLN (LayerNorm eps 1e-6, shift/scale) + FP8 row quant + FP8 QKV projection, T=32760 H=5120 I=15360"),
     "c4": dict(S=75600, latent=(21, 90, 160), desc="C4: Wan2.2-A14B 720x1280x81 self-attention, S=75600 (21x45x80 tokens), H=40 D=128"),
+    "ffn": dict(S=32760, latent=None, desc="Wan FFN of one block on the C2 token count: GELU_tanh(x @ Wu + bu) @ Wd + bd, x [32760, 5120], Wu [5120, 13824], Wd [13824, 5120], bf16"),
     "oproj": dict(S=32760, latent=None, desc="Output projection of one C2 self-attention layer (d-major [1,40,128,32760] @ [5120,5120] + bias) with the norm2 gated residual and adaLN (LayerNorm + FP8 row quant)"),
 }
 METRIC = "ring-attn TFLOP/s at S=32760 (one Wan2.2-A14B self-attention layer), CP=N"
@@ -212,6 +213,8 @@ def main():
         return run_c3(args, emit)
     if args.config == "oproj":
         return run_oproj(args, emit)
+    if args.config == "ffn":
+        return run_ffn(args, emit)
 
     import torch
     import torch.distributed as dist
@@ -614,6 +617,55 @@ def run_oproj(args, emit):
         },
         "clocks": clocks,
         "gpu_launches": 5 * n,
+    })
+
+
+def run_ffn(args, emit):
+    """The block's FFN (two tcgen05 GEMMs, GELU-tanh fused into the first epilogue)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module(PKG)
+    pkg.build()
+    lib = importlib.import_module(PKG + "._lib")
+    T, H, I = (args.tokens or 32760), HIDDEN, 13824
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(1, T, H, generator=g, device=dev).to(torch.bfloat16)
+    wu = (torch.randn(H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    bu = (torch.randn(1, I, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    bd = (torch.randn(1, H, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        pkg.wan_mlp(x, wu, wd, bu, bd)
+    torch.cuda.synchronize()
+    n = max(args.steps, 5)
+    sampler = ClockSampler(0)
+    sampler.start()
+    ts = []
+    for _ in range(n):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        pkg.wan_mlp(x, wu, wd, bu, bd)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    clocks = sampler.stop()
+    assert lib.device_status() == 0
+    t = statistics.median(ts)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    flops = 4.0 * T * H * I
+    emit({
+        "metric": "Wan FFN TFLOP/s (one block, C2 token count)", "value": round(flops / t / 1e9, 1), "unit": "TFLOP/s",
+        "ms_per_step": round(t, 4), "higher_is_better": True, "n_gpus": 1, "steps": n, "warmup": args.warmup,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": CONFIGS["ffn"]["desc"], "T": T, "H": H, "I": I, "l2": "flushed (256 MB write) before each call"},
+        "roofline": {"bound": "tensor", "achieved": round(flops / t / 1e9, 1), "peak": bf16, "unit": "TFLOP/s",
+                     "frac": round(flops / t / 1e9 / bf16, 4), "peak_source": "measured (bf16_tflops burst)"},
+        "clocks": clocks, "gpu_launches": 2 * n,
     })
 
 

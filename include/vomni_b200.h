@@ -171,7 +171,7 @@ VOMNI_API int vomni_qkv_unpack_rows(const void* packed, int t, int h, void* code
 
 /* ------------------------------------------------------------------ output projection
  * _wan_o_proj (diffusion/models/wan2_2/wan2_2_transformer.py:246-254) on the d-major attention output
- * attn [b, k, s] bf16 (k = heads*128; s % 8 == 0) and w [k, h] bf16 (h % 256 == 0, k % 64 == 0):
+ * attn [b, k, s] bf16 (k = heads*128; s % 8 == 0) and w [k, h] bf16 (h % 32 == 0, k % 64 == 0):
  * y = bf16(bf16(x @ w) + bias) with x[t] = attn[:, :, t], written to out [b, s, h]. With a residual
  * [b, s, h] bf16 the kernel writes the norm2 gated residual t = bf16(residual + gate * y) instead
  * (gate fp32 [b, h] when gate_per_batch, else [h]; NULL = 1), the residual step of
@@ -179,6 +179,12 @@ VOMNI_API int vomni_qkv_unpack_rows(const void* packed, int t, int h, void* code
 VOMNI_API int vomni_oproj_gemm(const void* attn, int b, int k, int s, const void* w, const void* bias, int h,
                                const void* residual, const float* gate, int gate_per_batch, void* out,
                                vomni_stream_t stream);
+
+/* Wan FFN GEMM step (_wan_mlp, wan2_2_transformer.py:389-410): out [m, n] = x [m, k] @ w [k, n] + bias,
+ * rounded to bf16 after the matmul and after the bias add as torch does; act = 1 then applies
+ * GELU-tanh (fp32 opmath, bf16 result). All bf16; k % 64 == 0, n % 32 == 0. */
+VOMNI_API int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, const void* bias, int n, int act,
+                             void* out, vomni_stream_t stream);
 
 /* ------------------------------------------------------------------ context-parallel ring
  * Replaces the ring driver of ring_attention_const_max_fwd(num_workers = N > 1)

@@ -12,8 +12,9 @@ cannot run without a Trainium toolchain):
   adaln_quant_torch.py), loaded by file path;
 * ``_eager_adaln`` (diffusion/quantization/adaln_kernels.py:51-84), loaded by file path;
 * ``WanRotaryPosEmbed`` / ``apply_rotary_emb_wan`` (diffusion/layers/rope.py), by file path;
-* ``_torch_attend`` (diffusion/models/wan2_2/wan2_2_transformer.py:640-650) and ``_wan_o_proj``
-  (:246-254, its torch path: the NKI kernel's capability check is stubbed to False),
+* ``_torch_attend`` (diffusion/models/wan2_2/wan2_2_transformer.py:640-650), ``_wan_o_proj``
+  (:246-254) and ``_wan_mlp`` (:389-410), the latter two on their torch path (the NKI kernels'
+  capability checks are stubbed to False),
   ``DistributedRMSNorm`` (:855-893), ``_rope_rotate_half_caches``
   (diffusion/quantization/row_mx_modules.py:51-76) and the de-interleave loaders
   (diffusion/quantization/row_mx_loaders.py:26-71): their modules import the Neuron SDK at
@@ -188,6 +189,24 @@ def gen_oproj():
     np.savez_compressed(OUT / "wan_o_proj.npz", **out)
 
 
+def gen_mlp():
+    wt = REF / "diffusion/models/wan2_2/wan2_2_transformer.py"
+    fns = _extract(wt, ["_wan_mlp"], {"torch": torch, "F": torch.nn.functional,
+                                      "_can_use_wan_mlp_kernel": lambda *a: False})
+    rng = torch.Generator().manual_seed(20261203)
+    out = {}
+    for tag, (B, T, H, I) in {"a": (1, 64, 128, 256), "b": (2, 24, 128, 256)}.items():
+        x = torch.randn(B, T, H, generator=rng).to(torch.bfloat16)
+        wu = (0.05 * torch.randn(H, I, generator=rng)).to(torch.bfloat16)
+        wd = (0.05 * torch.randn(I, H, generator=rng)).to(torch.bfloat16)
+        bu = (0.5 * torch.randn(1, I, generator=rng)).to(torch.bfloat16)
+        bd = (0.5 * torch.randn(1, H, generator=rng)).to(torch.bfloat16)
+        y = fns["_wan_mlp"](x, wu, wd, bu, bd)
+        out.update({f"{tag}|x": _bf16(x), f"{tag}|wu": _bf16(wu), f"{tag}|wd": _bf16(wd), f"{tag}|bu": _bf16(bu),
+                    f"{tag}|bd": _bf16(bd), f"{tag}|y": _bf16(y)})
+    np.savez_compressed(OUT / "wan_mlp.npz", **out)
+
+
 def main():
     if not REF.exists():
         sys.exit(f"reference checkout not found at {REF}")
@@ -202,6 +221,7 @@ def main():
     gen_attention(rng)
     gen_rope_norm(rng)
     gen_oproj()
+    gen_mlp()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

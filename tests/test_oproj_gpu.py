@@ -37,7 +37,7 @@ def test_golden_reference_outputs(pkg, dev, golden):
         assert _one_step(y.float().cpu().numpy(), g[f"{tag}|y"]) > 0.99
 
 
-@pytest.mark.parametrize("B,N,S,H", [(1, 4, 1000, 512), (2, 2, 136, 768), (1, 1, 8, 256), (1, 8, 4095, 1024)])
+@pytest.mark.parametrize("B,N,S,H", [(1, 4, 1000, 512), (2, 2, 136, 768), (1, 1, 8, 256), (1, 8, 4095, 1024), (1, 2, 64, 160)])
 def test_o_proj_vs_oracle(pkg, dev, B, N, S, H):
     rng = np.random.default_rng(B * 1000 + S)
     from oracle.numerics import bf16_round
@@ -90,4 +90,4 @@ def test_errors(pkg, dev):
         pkg.wan_o_proj(a, torch.zeros(128, 256, dtype=torch.bfloat16, device=dev), None)  # N*D mismatch
     lib = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200._lib")
     with pytest.raises(lib.VomniError):
-        pkg.wan_o_proj(a, torch.zeros(256, 200, dtype=torch.bfloat16, device=dev), None)  # H % 256
+        pkg.wan_o_proj(a, torch.zeros(256, 200, dtype=torch.bfloat16, device=dev), None)  # H % 32

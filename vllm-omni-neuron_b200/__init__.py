@@ -8,6 +8,7 @@ Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call AP
 * :func:`row_mx_qkv_proj` — FP8 QKV projection with across-heads RMS norm + rotate-half RoPE
 * :func:`wan_o_proj`, :func:`attn_out_norm2` — output projection of the d-major attention output,
   with the block's gated residual + norm2 adaLN
+* :func:`wan_mlp` — the block's FFN (GELU-tanh MLP)
 
 Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``) built by
 :func:`build`.
@@ -16,6 +17,7 @@ Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``
 from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .build import build
+from .ffn import wan_mlp
 from .leaf import wan_self_attention_fp8
 from .oproj import attn_out_norm2, o_proj_gated_residual, wan_o_proj
 from .qkv import (
@@ -43,6 +45,7 @@ __all__ = [
     "ring_attention_const_max_fwd",
     "row_mx_qkv_proj",
     "wan_cp_self_attention",
+    "wan_mlp",
     "wan_o_proj",
     "wan_self_attention_fp8",
 ]

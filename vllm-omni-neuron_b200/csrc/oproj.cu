@@ -14,6 +14,10 @@
 // its 128 output columns per 64-deep k-block (32 KB per stage, six stages). The epilogue rounds as
 // torch does, adds the bias, and with a residual writes t = bf16(residual + gate * y) instead of y,
 // so norm2 reads t once (the adaLN kernel then runs without its residual step).
+//
+// The same kernel with a K-major A operand (token rows, [M, K] row-major) and a GELU-tanh epilogue
+// runs the Wan FFN: _wan_mlp (wan2_2_transformer.py:389-410) = GELU_tanh(x @ Wu + bu) @ Wd + bd, each
+// step rounded to bf16 as torch does (the GELU in fp32 opmath on the bf16 input).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -33,7 +37,9 @@ constexpr uint32_t kBBytes = 2 * kChunkBytes;        // this CTA's 128 output co
 constexpr uint32_t kStageBytes = kABytes + kBBytes;  // 32 KB
 constexpr uint32_t kSmemBar = kStages * kStageBytes;
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;
-constexpr uint32_t kIdesc = idesc_bf16_mn(256, 256, true, true);
+constexpr uint32_t kIdescMN = idesc_bf16_mn(256, 256, true, true);   // A MN-major (d-major attention)
+constexpr uint32_t kIdescK = idesc_bf16_mn(256, 256, false, true);   // A K-major (token rows)
+enum Epi { EPI_BIAS = 0, EPI_RESIDUAL = 1, EPI_GELU = 2 };
 constexpr int kGroup = 8;
 
 struct Params {
@@ -63,8 +69,20 @@ VOMNI_DEV Tile tile_of(int t, const Params& p) {
   return Tile{band / p.m_bands, band % p.m_bands, r / rows};
 }
 
+// GELU with the tanh approximation in fp32, torch's formula (aten gelu kernel, approximate='tanh'):
+// 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3))).
+VOMNI_DEV float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float kKappa = 0.044715f;
+  const float x3 = x * x * x;
+  const float inner = kBeta * (x + kKappa * x3);
+  return 0.5f * x * (1.f + tanhf(inner));
+}
+
+// kAK: A is K-major ([M, K] rows, one 128-row box of 64 k per stage) instead of MN-major.
+template <bool kAK, int kEpi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    oproj_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmemBar);
@@ -124,8 +142,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + st * kStageBytes;
           const uint32_t bar = lead_full + st * 8;
           if (leader) mbar_expect_tx(&full[st], 2 * kStageBytes);
-          tma_load_3d_pair(&tmA, bar, sa, tok0, kb * kBK, tt.b);
-          tma_load_3d_pair(&tmA, bar, sa + kChunkBytes, tok0 + 64, kb * kBK, tt.b);
+          if (kAK) {
+            tma_load_2d_pair(&tmA, bar, sa, kb * kBK, tok0);
+          } else {
+            tma_load_3d_pair(&tmA, bar, sa, tok0, kb * kBK, tt.b);
+            tma_load_3d_pair(&tmA, bar, sa + kChunkBytes, tok0 + 64, kb * kBK, tt.b);
+          }
           tma_load_2d_pair(&tmB, bar, sa + kABytes, n0, kb * kBK);
           tma_load_2d_pair(&tmB, bar, sa + kABytes + kChunkBytes, n0 + 64, kb * kBK);
         }
@@ -134,8 +156,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (leader && lane == 0) {
       // MN-major SW128 operands: 64-element chunks kChunkBytes apart (LBO), 8-row K groups 1 KB
-      // apart (SBO); one K=16 step = 16 rows = +2 KB.
-      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), kChunkBytes, 1024, kLayoutSW128);
+      // apart (SBO); one K=16 step = 16 rows = +2 KB. K-major A: 128-byte rows of 64 k, 8-row
+      // groups 1 KB apart; one K=16 step = +32 B inside the swizzled row.
+      const uint64_t a_desc0 = kAK ? make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128)
+                                   : make_sdesc(smem_u32(smem), kChunkBytes, 1024, kLayoutSW128);
+      const uint64_t b_desc0 = make_sdesc(smem_u32(smem + kABytes), kChunkBytes, 1024, kLayoutSW128);
       uint32_t it = 0;
       int lt = 0;
       bool ok = true;
@@ -153,10 +178,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint64_t ad0 = a_desc0 + ((st * kStageBytes) >> 4);
-          const uint64_t bd0 = ad0 + (kABytes >> 4);
+          const uint64_t bd0 = b_desc0 + ((st * kStageBytes) >> 4);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
-            mma_f16_ss_pair(tacc, ad0 + ((k * 2048) >> 4), bd0 + ((k * 2048) >> 4), kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_f16_ss_pair(tacc, ad0 + ((k * (kAK ? 32 : 2048)) >> 4), bd0 + ((k * 2048) >> 4), kAK ? kIdescK : kIdescMN,
+                            (kb > 0 || k > 0) ? 1u : 0u);
           tc_commit_pair(&empty[st]);
         }
         if (ok) tc_commit_pair(&acc_full[acc]);
@@ -183,8 +209,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld32(tacc + c * 32, r);
         tmem_ld_wait(r);
-        if (!row_ok) continue;
         const int col0 = n0 + c * 32;
+        if (!row_ok || col0 >= p.H) continue;  // rows past S, columns past H (H % 32 == 0)
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[i])));  // torch matmul out
@@ -202,7 +228,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (p.residual) {
+        if (kEpi == EPI_GELU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+        }
+        if (kEpi == EPI_RESIDUAL && p.residual) {
           const uint4* r4 = reinterpret_cast<const uint4*>(p.residual + orow + col0);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -237,6 +267,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+int ensure_smem_attr() {
+  static bool done = false;
+  if (!done) {
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<false, EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<false, EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    done = true;
+  }
+  return VOMNI_OK;
+}
+
 }  // namespace oproj
 }  // namespace vomni
 
@@ -247,7 +289,7 @@ extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const voi
                                 vomni_stream_t stream) {
   if (!attn || !w || !out) return VOMNI_EINVAL;
   if (gate && !residual) return VOMNI_EINVAL;
-  if (b <= 0 || s <= 0 || k <= 0 || h <= 0 || (k % oproj::kBK) || (h % 256)) return VOMNI_EBADSHAPE;
+  if (b <= 0 || s <= 0 || k <= 0 || h <= 0 || (k % oproj::kBK) || (h % 32)) return VOMNI_EBADSHAPE;
   if ((s % 8) || b > 65535) return VOMNI_EBADSHAPE;  // token rows of the d-major input must be 16-byte pitched
   const uintptr_t al = reinterpret_cast<uintptr_t>(attn) | reinterpret_cast<uintptr_t>(w) |
                        reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(residual) |
@@ -267,21 +309,60 @@ extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const voi
   p.K = k;
   p.H = h;
   p.m_bands = (s + 255) / 256;
-  p.n_tiles = h / 256;
+  p.n_tiles = (h + 255) / 256;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.gate = gate;
   p.gate_per_batch = gate_per_batch ? 1 : 0;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.status = device_status_ptr();
-  static bool attr = false;
-  if (!attr) {
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(oproj::oproj_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, oproj::kSmemBytes));
-    attr = true;
-  }
   const long long tiles = static_cast<long long>(b) * p.m_bands * p.n_tiles;
   const int pairs = static_cast<int>(tiles < num_sms() / 2 ? tiles : num_sms() / 2);
-  oproj::oproj_pair_kernel<<<2 * pairs, oproj::kThreads, oproj::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  rc = oproj::ensure_smem_attr();
+  if (rc) return rc;
+  auto kern = residual ? oproj::gemm_bf16_pair_kernel<false, oproj::EPI_RESIDUAL>
+                       : oproj::gemm_bf16_pair_kernel<false, oproj::EPI_BIAS>;
+  kern<<<2 * pairs, oproj::kThreads, oproj::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+extern "C" int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, const void* bias, int n, int act,
+                              void* out, vomni_stream_t stream) {
+  if (!x || !w || !out) return VOMNI_EINVAL;
+  if (m <= 0 || k <= 0 || n <= 0 || (k % oproj::kBK) || (n % 32) || act < 0 || act > 1) return VOMNI_EBADSHAPE;
+  if (m > 0x7fffffffLL) return VOMNI_EBADSHAPE;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                       reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(out);
+  if (al & 15) return VOMNI_EALIGN;
+  int rc = require_sm100();
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  rc = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
+                    static_cast<uint64_t>(k) * 2, 64, 128);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, static_cast<uint64_t>(n), static_cast<uint64_t>(k),
+                    static_cast<uint64_t>(n) * 2, 64, 64);
+  if (rc) return rc;
+  oproj::Params p;
+  p.B = 1;
+  p.S = static_cast<int>(m);
+  p.K = k;
+  p.H = n;
+  p.m_bands = static_cast<int>((m + 255) / 256);
+  p.n_tiles = (n + 255) / 256;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.residual = nullptr;
+  p.gate = nullptr;
+  p.gate_per_batch = 0;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.status = device_status_ptr();
+  rc = oproj::ensure_smem_attr();
+  if (rc) return rc;
+  const long long tiles = static_cast<long long>(p.m_bands) * p.n_tiles;
+  const int pairs = static_cast<int>(tiles < num_sms() / 2 ? tiles : num_sms() / 2);
+  auto kern = act ? oproj::gemm_bf16_pair_kernel<true, oproj::EPI_GELU> : oproj::gemm_bf16_pair_kernel<true, oproj::EPI_BIAS>;
+  kern<<<2 * pairs, oproj::kThreads, oproj::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }

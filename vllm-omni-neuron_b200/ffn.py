@@ -1,0 +1,43 @@
+"""Wan FFN on B200: the reference's ``_wan_mlp(hidden, up_weight, down_weight, up_bias, down_bias)``
+(vllm_omni_neuron/diffusion/models/wan2_2/wan2_2_transformer.py:389-410):
+``GELU_tanh(hidden @ up_weight + up_bias) @ down_weight + down_bias`` with torch's bf16 rounding
+after each matmul and bias add, the GELU in fp32 opmath. Two CTA-pair tcgen05 GEMMs; the first
+applies the bias and GELU-tanh in its epilogue, so the ``[T, I]`` intermediate is written once, bf16.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _gemm(x2: torch.Tensor, w: torch.Tensor, bias, act: int) -> torch.Tensor:
+    m, k = x2.shape
+    k2, n = w.shape
+    if k != k2:
+        raise ValueError(f"inner dims differ: {k} vs {k2}")
+    b = bias.reshape(-1).to(torch.bfloat16).contiguous() if bias is not None else None
+    if b is not None and b.numel() != n:
+        raise ValueError(f"bias has {b.numel()} values for {n} columns")
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=x2.device)
+    _lib.check(
+        _lib.load().vomni_ffn_gemm(x2.data_ptr(), m, k, w.data_ptr(), b.data_ptr() if b is not None else None, n, act,
+                                   out.data_ptr(), torch.cuda.current_stream(x2.device).cuda_stream),
+        "vomni_ffn_gemm",
+    )
+    return out
+
+
+def wan_mlp(hidden: torch.Tensor, up_weight: torch.Tensor, down_weight: torch.Tensor, up_bias, down_bias) -> torch.Tensor:
+    """``[B, T, H]`` bf16 -> ``[B, T, H_out]`` bf16."""
+    for name, t in (("hidden", hidden), ("up_weight", up_weight), ("down_weight", down_weight)):
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor (the B200 kernel has no CPU path)")
+    lead = tuple(hidden.shape[:-1])
+    x2 = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+    up = _gemm(x2, up_weight.contiguous(), up_bias, 1)
+    out = _gemm(up, down_weight.contiguous(), down_bias, 0)
+    return out.reshape(lead + (down_weight.shape[1],))
