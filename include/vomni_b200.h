@@ -111,6 +111,14 @@ VOMNI_API int vomni_cm_attention_local_strided(const void* q, const void* k, con
                                                int s, int h, int d, long long q_stride, long long kv_stride,
                                                float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
                                                vomni_stream_t stream);
+/* Cross-attention (keys from another sequence, e.g. the 512-token text context; no ring): the
+ * exact attention of _nki_attend / _torch_attend (wan2_2_transformer.py:640-674) over s_kv keys, via
+ * the same const-max kernel. q [b, s_q, h, d] and k, v [b, s_kv, h, d] token-major (token pitches
+ * q_stride / kv_stride elements, 0 = dense); workspace as vomni_cm_workspace_bytes(b, s_q, h, d). */
+VOMNI_API int vomni_cm_attention_cross(const void* q, const void* k, const void* v, void* out, float* lse, int b,
+                                       int s_q, int s_kv, int h, int d, long long q_stride, long long kv_stride,
+                                       float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
+                                       vomni_stream_t stream);
 
 /* Single-rank (num_workers == 1) const-max attention: prologue + one final pass.
  * Replaces ring_attention_const_max_fwd(num_workers=1) (ring_attention_const_max_fwd.py:1306-1327).
@@ -182,9 +190,19 @@ VOMNI_API int vomni_oproj_gemm(const void* attn, int b, int k, int s, const void
 
 /* Wan FFN GEMM step (_wan_mlp, wan2_2_transformer.py:389-410): out [m, n] = x [m, k] @ w [k, n] + bias,
  * rounded to bf16 after the matmul and after the bias add as torch does; act = 1 then applies
- * GELU-tanh (fp32 opmath, bf16 result). All bf16; k % 64 == 0, n % 32 == 0. */
+ * GELU-tanh (fp32 opmath, bf16 result). With a residual [m, n] (act = 0) the kernel writes the block's
+ * closing gated residual bf16(residual + gate * y) instead (wan2_2_transformer.py:1510-1512; gate fp32
+ * [m / gate_rows, n], row r using gate row r / gate_rows; NULL = 1). All bf16; k % 64 == 0, n % 32 == 0. */
 VOMNI_API int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, const void* bias, int n, int act,
-                             void* out, vomni_stream_t stream);
+                             const void* residual, const float* gate, long long gate_rows, void* out,
+                             vomni_stream_t stream);
+
+/* bf16 projection for the across-heads RMS norm that follows (the bf16 self-attention leaf's
+ * qkv_proj + norm_q/norm_k, wan2_2_transformer.py:1097-1109, and the cross-attention's q/k
+ * projections, :1232-1248): out [m, n] = bf16(bf16(x @ w) + bias) and sumsq [m, n_norm_heads] = per
+ * 128-column head sums of squares of the stored values, the input of vomni_qk_norm_rope. */
+VOMNI_API int vomni_linear_sumsq(const void* x, long long m, int k, const void* w, const void* bias, int n,
+                                 float* sumsq, int n_norm_heads, void* out, vomni_stream_t stream);
 
 /* ------------------------------------------------------------------ context-parallel ring
  * Replaces the ring driver of ring_attention_const_max_fwd(num_workers = N > 1)

@@ -9,6 +9,7 @@ Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call AP
 * :func:`wan_o_proj`, :func:`attn_out_norm2` — output projection of the d-major attention output,
   with the block's gated residual + norm2 adaLN
 * :func:`wan_mlp` — the block's FFN (GELU-tanh MLP)
+* :func:`wan_block_forward` — a whole transformer block (self-attn + cross-attn + FFN, bf16 leaves)
 
 Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``) built by
 :func:`build`.
@@ -16,6 +17,7 @@ Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``
 
 from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
+from .block import BlockWeights, prepare_block_weights, project_cross_kv, wan_block_forward
 from .build import build
 from .ffn import wan_mlp
 from .leaf import wan_self_attention_fp8
@@ -31,6 +33,7 @@ from .qkv import (
 from .ring import destroy_rings
 
 __all__ = [
+    "BlockWeights",
     "adaln_modulate",
     "attention_local",
     "attn_out_norm2",
@@ -39,11 +42,14 @@ __all__ = [
     "mx32_qkv_proj",
     "o_proj_gated_residual",
     "pack_mx_scales",
+    "prepare_block_weights",
+    "project_cross_kv",
     "quantize_qkv_weight",
     "quantize_qkv_weight_mx32",
     "repack_mx_contiguous",
     "ring_attention_const_max_fwd",
     "row_mx_qkv_proj",
+    "wan_block_forward",
     "wan_cp_self_attention",
     "wan_mlp",
     "wan_o_proj",

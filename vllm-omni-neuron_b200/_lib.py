@@ -41,7 +41,8 @@ SIGNATURES = {
     "vomni_qkv_fp8_gemm": (c_int, [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P]),
     "vomni_qk_norm_rope": (c_int, [P, c_int, c_int, c_int, c_int, c_int, P, c_float, P, P, P, P, P]),
     "vomni_oproj_gemm": (c_int, [P, c_int, c_int, c_int, P, P, c_int, P, P, c_int, P, P]),
-    "vomni_ffn_gemm": (c_int, [P, ctypes.c_longlong, c_int, P, P, c_int, c_int, P, P]),
+    "vomni_ffn_gemm": (c_int, [P, ctypes.c_longlong, c_int, P, P, c_int, c_int, P, P, ctypes.c_longlong, P, P]),
+    "vomni_linear_sumsq": (c_int, [P, ctypes.c_longlong, c_int, P, P, c_int, P, c_int, P, P]),
     "vomni_qkv_unpack_rows": (c_int, [P, c_int, c_int, P, P, P]),
     "vomni_mx_packed_scales_bytes": (c_size_t, [c_int, c_int]),
     "vomni_mx_pack_scales": (c_int, [P, c_int, c_int, P, P]),
@@ -64,6 +65,11 @@ SIGNATURES = {
     "vomni_cm_attention_local_strided": (
         c_int,
         [P, P, P, P, P, c_int, c_int, c_int, c_int, ctypes.c_longlong, ctypes.c_longlong, c_float, c_int, P, c_size_t, P],
+    ),
+    "vomni_cm_attention_cross": (
+        c_int,
+        [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, ctypes.c_longlong, ctypes.c_longlong, c_float, c_int, P,
+         c_size_t, P],
     ),
     "vomni_ring_attention_strided": (
         c_int,

@@ -612,30 +612,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // per-head max of ||k||^2 folded through shared memory into kmax2 (atomicMax on the float bits,
 // valid because sums of squares are non-negative).
 __global__ void cm_norms_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, int b, int s,
-                                int h, long long q_stride, long long k_stride, float* __restrict__ qn2,
+                                int s_k, int h, long long q_stride, long long k_stride, float* __restrict__ qn2,
                                 unsigned int* __restrict__ kmax2_bits) {
+  // q rows: b*s*h (per-token ||q||^2); k rows: b*s_k*h (per-head max ||k||^2). s_k != s for
+  // cross-attention (keys from another sequence).
   extern __shared__ unsigned int smax[];  // [b*h]
   const int bhn = b * h;
   for (int i = threadIdx.x; i < bhn; i += blockDim.x) smax[i] = 0u;
   __syncthreads();
-  const long long rows = static_cast<long long>(b) * s * h;
+  const long long rows_q = static_cast<long long>(b) * s * h;
+  const long long rows_k = static_cast<long long>(b) * s_k * h;
+  const long long rows = rows_q > rows_k ? rows_q : rows_k;
   const int half = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
   const int sub = threadIdx.x & 15;
   const unsigned hmask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
   const int halves = (gridDim.x * blockDim.x) >> 4;
   for (long long r = half; r < rows; r += halves) {
-    const long long tok_r = r / h, hd = (r % h) * kD;  // token-major rows, tokens `stride` apart
-    const uint4 qv = reinterpret_cast<const uint4*>(q + tok_r * q_stride + hd)[sub];
-    const uint4 kv = reinterpret_cast<const uint4*>(k + tok_r * k_stride + hd)[sub];
+    const long long hd = (r % h) * kD;
+    const int hh = static_cast<int>(r % h);
     float sq = 0.f, sk = 0.f;
-    const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qv);
-    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
+    if (r < rows_q) {
+      const uint4 qv = reinterpret_cast<const uint4*>(q + (r / h) * q_stride + hd)[sub];
+      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qv);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 a = __bfloat1622float2(q2[i]);
-      const float2 c = __bfloat1622float2(k2[i]);
-      sq = fmaf(a.x, a.x, fmaf(a.y, a.y, sq));
-      sk = fmaf(c.x, c.x, fmaf(c.y, c.y, sk));
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = __bfloat1622float2(q2[i]);
+        sq = fmaf(a.x, a.x, fmaf(a.y, a.y, sq));
+      }
+    }
+    if (r < rows_k) {
+      const uint4 kv = reinterpret_cast<const uint4*>(k + (r / h) * k_stride + hd)[sub];
+      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 c = __bfloat1622float2(k2[i]);
+        sk = fmaf(c.x, c.x, fmaf(c.y, c.y, sk));
+      }
     }
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) {
@@ -643,12 +655,11 @@ __global__ void cm_norms_kernel(const __nv_bfloat16* __restrict__ q, const __nv_
       sk += __shfl_xor_sync(hmask, sk, o);
     }
     if (sub == 0) {
-      const int hh = static_cast<int>(r % h);
-      const long long tok = r / h;
-      const int bb = static_cast<int>(tok / s);
-      const int ss = static_cast<int>(tok % s);
-      qn2[(static_cast<size_t>(bb) * h + hh) * s + ss] = sq;
-      atomicMax(&smax[bb * h + hh], __float_as_uint(sk));
+      if (r < rows_q) {
+        const long long tok = r / h;
+        qn2[(static_cast<size_t>(tok / s) * h + hh) * s + tok % s] = sq;
+      }
+      if (r < rows_k) atomicMax(&smax[static_cast<int>((r / h) / s_k) * h + hh], __float_as_uint(sk));
     }
   }
   __syncthreads();
@@ -669,10 +680,10 @@ extern "C" size_t vomni_cm_workspace_bytes(int b, int s, int h, int d) {
   return align_up(qn, 256) + align_up(km, 256);
 }
 
-extern "C" int vomni_cm_prologue_strided(const void* q, const void* k, int b, int s, int h, int d, long long q_stride,
-                                         long long k_stride, float* qn2, float* kmax2, vomni_stream_t stream) {
+static int cm_prologue(const void* q, const void* k, int b, int s, int s_k, int h, int d, long long q_stride,
+                       long long k_stride, float* qn2, float* kmax2, vomni_stream_t stream) {
   if (!q || !k || !qn2 || !kmax2) return VOMNI_EINVAL;
-  if (d != cm::kD || b <= 0 || s <= 0 || h <= 0) return VOMNI_EBADSHAPE;
+  if (d != cm::kD || b <= 0 || s <= 0 || s_k <= 0 || h <= 0) return VOMNI_EBADSHAPE;
   if (b * h > 8192) return VOMNI_EBADSHAPE;
   if (q_stride == 0) q_stride = static_cast<long long>(h) * d;
   if (k_stride == 0) k_stride = static_cast<long long>(h) * d;
@@ -681,16 +692,21 @@ extern "C" int vomni_cm_prologue_strided(const void* q, const void* k, int b, in
     return VOMNI_EALIGN;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   VOMNI_CUDA_TRY(cudaMemsetAsync(kmax2, 0, sizeof(float) * b * h, st));
-  const long long rows = static_cast<long long>(b) * s * h;
+  const long long rows = static_cast<long long>(b) * (s > s_k ? s : s_k) * h;
   const int threads = 256;
   long long blocks = (rows * 16 + threads - 1) / threads;
   const int max_blocks = num_sms() * 8;
   if (blocks > max_blocks) blocks = max_blocks;
   cm::cm_norms_kernel<<<static_cast<int>(blocks), threads, sizeof(unsigned) * b * h, st>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), b, s, h, q_stride, k_stride, qn2,
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), b, s, s_k, h, q_stride, k_stride, qn2,
       reinterpret_cast<unsigned int*>(kmax2));
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
+}
+
+extern "C" int vomni_cm_prologue_strided(const void* q, const void* k, int b, int s, int h, int d, long long q_stride,
+                                         long long k_stride, float* qn2, float* kmax2, vomni_stream_t stream) {
+  return cm_prologue(q, k, b, s, s, h, d, q_stride, k_stride, qn2, kmax2, stream);
 }
 
 extern "C" int vomni_cm_prologue(const void* q, const void* k, int b, int s, int h, int d, float* qn2, float* kmax2,
@@ -804,6 +820,24 @@ extern "C" int vomni_cm_attention_local_strided(const void* q, const void* k, co
   if (rc) return rc;
   return vomni_cm_attend_strided(q, k, v, b, s, s, 0, s, h, d, q_stride, kv_stride, softmax_scale, qn2, kmax2, nullptr,
                                  nullptr, flags | VOMNI_CM_FINAL, out, lse, stream);
+}
+
+extern "C" int vomni_cm_attention_cross(const void* q, const void* k, const void* v, void* out, float* lse, int b,
+                                        int s_q, int s_kv, int h, int d, long long q_stride, long long kv_stride,
+                                        float softmax_scale, int flags, void* workspace, size_t workspace_bytes,
+                                        vomni_stream_t stream) {
+  if (!workspace) return VOMNI_EINVAL;
+  if (flags & ~(VOMNI_CM_OUT_DMAJOR | VOMNI_CM_LSE)) return VOMNI_EINVAL;
+  const size_t need = vomni_cm_workspace_bytes(b, s_q, h, d);
+  if (need == 0 || s_kv <= 0) return VOMNI_EBADSHAPE;
+  if (workspace_bytes < need) return VOMNI_EWORKSPACE;
+  float* qn2 = static_cast<float*>(workspace);
+  float* kmax2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                          align_up(static_cast<size_t>(b) * h * s_q * sizeof(float), 256));
+  int rc = cm_prologue(q, k, b, s_q, s_kv, h, d, q_stride, kv_stride, qn2, kmax2, stream);
+  if (rc) return rc;
+  return vomni_cm_attend_strided(q, k, v, b, s_q, s_kv, 0, s_kv, h, d, q_stride, kv_stride, softmax_scale, qn2, kmax2,
+                                 nullptr, nullptr, flags | VOMNI_CM_FINAL, out, lse, stream);
 }
 
 extern "C" int vomni_cm_attention_local(const void* q, const void* k, const void* v, void* out, float* lse, int b, int s,

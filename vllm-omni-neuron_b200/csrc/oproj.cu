@@ -39,7 +39,9 @@ constexpr uint32_t kSmemBar = kStages * kStageBytes;
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;
 constexpr uint32_t kIdescMN = idesc_bf16_mn(256, 256, true, true);   // A MN-major (d-major attention)
 constexpr uint32_t kIdescK = idesc_bf16_mn(256, 256, false, true);   // A K-major (token rows)
-enum Epi { EPI_BIAS = 0, EPI_RESIDUAL = 1, EPI_GELU = 2 };
+// Epilogues: bias; bias + gated residual; bias + GELU-tanh; bias + per-head sums of squares of the
+// stored bf16 values (the input of the across-heads RMS norm, like the FP8 QKV GEMM's).
+enum Epi { EPI_BIAS = 0, EPI_RESIDUAL = 1, EPI_GELU = 2, EPI_SUMSQ = 3 };
 constexpr int kGroup = 8;
 
 struct Params {
@@ -50,6 +52,9 @@ struct Params {
   const __nv_bfloat16* residual;  // [B, S, H] or null
   const float* gate;              // [B, H] or [H] (gate_per_batch = 0) or null
   int gate_per_batch;
+  int gate_rows;  // > 0: gate row = output row / gate_rows (rows of one batch element in a flat [M, H])
+  float* sumsq;       // EPI_SUMSQ: [M, n_norm_heads]
+  int n_norm_heads;   // 128-column heads covered by sumsq (the Q and K segments)
   __nv_bfloat16* out;  // [B, S, H]
   int* status;
 };
@@ -202,8 +207,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool row_ok = tok < p.S;
       const int n0 = tt.nb * 256;
       const size_t orow = (static_cast<size_t>(tt.b) * p.S + tok) * p.H;
-      const float* gate = p.gate ? p.gate + (p.gate_per_batch ? static_cast<size_t>(tt.b) * p.H : 0) : nullptr;
+      const size_t grow_g = p.gate_rows > 0 ? static_cast<size_t>(tok / p.gate_rows) : (p.gate_per_batch ? tt.b : 0);
+      const float* gate = p.gate ? p.gate + grow_g * p.H : nullptr;
       const uint32_t tacc = tbase + lane_addr + acc * 256;
+      float ss = 0.f;
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
         uint32_t r[32];
@@ -253,6 +260,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 4; ++i)
           dst[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
                               pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+        if (kEpi == EPI_SUMSQ) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float q = __bfloat162float(__float2bfloat16_rn(v[i]));  // the stored value
+            ss = fmaf(q, q, ss);
+          }
+          const int head = col0 / 128;
+          if ((c & 3) == 3) {  // one 128-column head done
+            if (p.sumsq && head < p.n_norm_heads) p.sumsq[static_cast<size_t>(tok) * p.n_norm_heads + head] = ss;
+            ss = 0.f;
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -274,6 +293,8 @@ int ensure_smem_attr() {
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<false, EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_SUMSQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     done = true;
   }
   return VOMNI_OK;
@@ -314,6 +335,9 @@ extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const voi
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.gate = gate;
   p.gate_per_batch = gate_per_batch ? 1 : 0;
+  p.gate_rows = 0;
+  p.sumsq = nullptr;
+  p.n_norm_heads = 0;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.status = device_status_ptr();
   const long long tiles = static_cast<long long>(b) * p.m_bands * p.n_tiles;
@@ -327,13 +351,16 @@ extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const voi
   return VOMNI_OK;
 }
 
-extern "C" int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, const void* bias, int n, int act,
-                              void* out, vomni_stream_t stream) {
+static int bf16_linear(const void* x, long long m, int k, const void* w, const void* bias, int n, int act,
+                       const void* residual, const float* gate, long long gate_rows, float* sumsq, int n_norm_heads,
+                       void* out, vomni_stream_t stream) {
   if (!x || !w || !out) return VOMNI_EINVAL;
+  if ((gate && !residual) || (residual && act) || gate_rows < 0 || gate_rows > 0x7fffffffLL) return VOMNI_EINVAL;
   if (m <= 0 || k <= 0 || n <= 0 || (k % oproj::kBK) || (n % 32) || act < 0 || act > 1) return VOMNI_EBADSHAPE;
   if (m > 0x7fffffffLL) return VOMNI_EBADSHAPE;
   const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
-                       reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(out);
+                       reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(residual) |
+                       reinterpret_cast<uintptr_t>(out);
   if (al & 15) return VOMNI_EALIGN;
   int rc = require_sm100();
   if (rc) return rc;
@@ -352,17 +379,35 @@ extern "C" int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, 
   p.m_bands = static_cast<int>((m + 255) / 256);
   p.n_tiles = (n + 255) / 256;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
-  p.residual = nullptr;
-  p.gate = nullptr;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.gate = gate;
   p.gate_per_batch = 0;
+  p.gate_rows = static_cast<int>(gate_rows);
+  p.sumsq = sumsq;
+  p.n_norm_heads = n_norm_heads;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.status = device_status_ptr();
   rc = oproj::ensure_smem_attr();
   if (rc) return rc;
   const long long tiles = static_cast<long long>(p.m_bands) * p.n_tiles;
   const int pairs = static_cast<int>(tiles < num_sms() / 2 ? tiles : num_sms() / 2);
-  auto kern = act ? oproj::gemm_bf16_pair_kernel<true, oproj::EPI_GELU> : oproj::gemm_bf16_pair_kernel<true, oproj::EPI_BIAS>;
+  auto kern = act ? oproj::gemm_bf16_pair_kernel<true, oproj::EPI_GELU>
+                  : (residual ? oproj::gemm_bf16_pair_kernel<true, oproj::EPI_RESIDUAL>
+                              : (sumsq ? oproj::gemm_bf16_pair_kernel<true, oproj::EPI_SUMSQ>
+                                       : oproj::gemm_bf16_pair_kernel<true, oproj::EPI_BIAS>));
   kern<<<2 * pairs, oproj::kThreads, oproj::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
+}
+
+extern "C" int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, const void* bias, int n, int act,
+                              const void* residual, const float* gate, long long gate_rows, void* out,
+                              vomni_stream_t stream) {
+  return bf16_linear(x, m, k, w, bias, n, act, residual, gate, gate_rows, nullptr, 0, out, stream);
+}
+
+extern "C" int vomni_linear_sumsq(const void* x, long long m, int k, const void* w, const void* bias, int n,
+                                  float* sumsq, int n_norm_heads, void* out, vomni_stream_t stream) {
+  if (!sumsq || n_norm_heads < 0 || n_norm_heads * 128 > n) return VOMNI_EINVAL;
+  return bf16_linear(x, m, k, w, bias, n, 0, nullptr, nullptr, 0, sumsq, n_norm_heads, out, stream);
 }
