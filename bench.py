@@ -38,6 +38,7 @@ CONFIGS = {
     "c2": dict(S=32760, latent=(21, 60, 104), desc="C2: Wan2.2-A14B 480x832x81 self-attention, S=32760 (21x30x52 tokens), H=40 D=128"),
     "c3": dict(S=32760, latent=None, desc="C3: fused adaLN (LayerNorm eps 1e-6, shift/scale) + FP8 row quant + FP8 QKV projection, T=32760 H=5120 I=15360"),
     "c4": dict(S=75600, latent=(21, 90, 160), desc="C4: Wan2.2-A14B 720x1280x81 self-attention, S=75600 (21x45x80 tokens), H=40 D=128"),
+    "c5": dict(S=32760, latent=(21, 60, 104), desc="C5: CFG-parallel Wan2.2-A14B transformer block (self-attn + cross-attn to 512 text tokens + FFN 5120-13824-5120 GELU-tanh), bf16, B=2 (cond/uncond) split CFGP=2 x CP=N/2 (N=1: one branch, CP=1)"),
     "ffn": dict(S=32760, latent=None, desc="Wan FFN of one block on the C2 token count: GELU_tanh(x @ Wu + bu) @ Wd + bd, x [32760, 5120], Wu [5120, 13824], Wd [13824, 5120], bf16"),
     "oproj": dict(S=32760, latent=None, desc="Output projection of one C2 self-attention layer (d-major [1,40,128,32760] @ [5120,5120] + bias) with the norm2 gated residual and adaLN (LayerNorm + FP8 row quant)"),
 }
@@ -215,6 +216,8 @@ def main():
         return run_oproj(args, emit)
     if args.config == "ffn":
         return run_ffn(args, emit)
+    if args.config == "c5":
+        return run_c5(args, world, rank, local_rank, emit)
 
     import torch
     import torch.distributed as dist
@@ -667,6 +670,112 @@ def run_ffn(args, emit):
                      "frac": round(flops / t / 1e9 / bf16, 4), "peak_source": "measured (bf16_tflops burst)"},
         "clocks": clocks, "gpu_launches": 2 * n,
     })
+
+
+def c5_block_flops(S: int, L: int = 512, I: int = 13824) -> float:
+    """Algorithmic FLOPs of one block for one CFG branch (text K/V projection excluded: once per generation)."""
+    H = HIDDEN
+    return (4.0 * HEADS * S * S * HEAD_DIM + 2.0 * S * H * 3 * H + 2.0 * S * H * H + 2 * 2.0 * S * H * H
+            + 4.0 * HEADS * S * L * HEAD_DIM + 4.0 * S * H * I)
+
+
+def run_c5(args, world, rank, local_rank, emit):
+    """Config 5: one transformer block per CFG branch. N=1: one branch at CP=1 (the single-GPU case);
+    N>1: CFGP=2 x CP=N/2, ranks [0, N/2) run the cond branch and [N/2, N) the uncond one, each CP group
+    a const-max ring over its own sequence shards (replica groups as get_cp_replica_groups builds them)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        if world % 2:
+            raise SystemExit("config c5 needs an even GPU count (CFGP=2)")
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    cp = max(world // 2, 1)
+    branch = rank // cp if world > 1 else 0
+    cp_rank = rank % cp
+    groups = tuple(tuple(range(g * cp, (g + 1) * cp)) for g in range(2)) if world > 1 else None
+    pkg = importlib.import_module(PKG)
+    pkg.build()
+    lib = importlib.import_module(PKG + "._lib")
+    rope = importlib.import_module(PKG + ".rope")
+    S, H, I, L = CONFIGS["c5"]["S"], HIDDEN, 13824, 512
+    s_loc = S // cp
+    g = torch.Generator(device=dev).manual_seed(1234)  # same weights on every rank
+    rn = lambda *shape, s=0.02: (torch.randn(*shape, generator=g, device=dev) * s).to(torch.bfloat16)
+    w = {
+        "scale_shift_table": torch.randn(1, 6, H, generator=g, device=dev) / math.sqrt(H),
+        "attn1.qkv_proj_weight": rn(H, 3 * H), "attn1.qkv_proj_bias": rn(3 * H),
+        "attn1.norm_q.weight": 1 + rn(H, s=0.1), "attn1.norm_k.weight": 1 + rn(H, s=0.1),
+        "attn1.o_proj_weight": rn(H, H), "attn1.o_proj_bias": rn(H),
+        "norm2.weight": 1 + rn(H, s=0.1), "norm2.bias": rn(H),
+        "attn2.q_proj_weight": rn(H, H), "attn2.q_proj_bias": rn(H), "attn2.norm_q.weight": 1 + rn(H, s=0.1),
+        "attn2.k_proj_weight": rn(H, H), "attn2.k_proj_bias": rn(H), "attn2.norm_k.weight": 1 + rn(H, s=0.1),
+        "attn2.v_proj_weight": rn(H, H), "attn2.v_proj_bias": rn(H),
+        "attn2.o_proj_weight": rn(H, H), "attn2.o_proj_bias": rn(H),
+        "ffn.up_weight": rn(H, I), "ffn.up_bias": rn(I), "ffn.down_weight": rn(I, H), "ffn.down_bias": rn(H),
+    }
+    bw = pkg.prepare_block_weights(w, HEADS)
+    # this branch's inputs: hidden ~ N(0,1), text context ~ N(0,1) already projected to 5120 (the text
+    # embedding runs once per generation, outside the block), timestep embedding ~ N(0, 0.1)
+    gb = torch.Generator(device=dev).manual_seed(99 + branch)
+    hidden = torch.randn(1, S, H, generator=gb, device=dev)[:, cp_rank * s_loc:(cp_rank + 1) * s_loc].to(torch.bfloat16).contiguous()
+    ctx = torch.randn(1, L, H, generator=gb, device=dev).to(torch.bfloat16)
+    temb = torch.randn(1, 6, H, generator=gb, device=dev) * 0.1
+    kv = pkg.project_cross_kv(ctx, w["attn2.k_proj_weight"], w["attn2.k_proj_bias"], w["attn2.norm_k.weight"],
+                              w["attn2.v_proj_weight"], w["attn2.v_proj_bias"], HEADS)
+    cos, sin = rope.wan_rotary_freqs(HEAD_DIM, (1, 2, 2), 1024, CONFIGS["c5"]["latent"], device=dev)
+    cos_rh, sin_rh = rope.rope_rotate_half_caches(cos, sin)
+    cos_rh = cos_rh.reshape(S, HEAD_DIM)[cp_rank * s_loc:(cp_rank + 1) * s_loc].contiguous()
+    sin_rh = sin_rh.reshape(S, HEAD_DIM)[cp_rank * s_loc:(cp_rank + 1) * s_loc].contiguous()
+
+    def step():
+        return pkg.wan_block_forward(hidden, temb, (cos_rh, sin_rh), kv, bw, cp_size=cp,
+                                     cp_group=None, cp_replica_groups=groups)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = step()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert lib.device_status() == 0 and torch.isfinite(out.float()).all()
+    branches = 2 if world > 1 else 1
+    flops = branches * c5_block_flops(S)
+    if rank == 0:
+        emit({
+            "metric": "Wan2.2 transformer block TFLOP/s (whole job; CFGP=2 x CP=N/2)", "value": round(flops / ms / 1e9, 1),
+            "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights ~N(0,0.02), hidden/text ~N(0,1))",
+            "config": {"workload": CONFIGS["c5"]["desc"], "S": S, "branches": branches, "cp": cp, "s_loc": s_loc,
+                       "flops_per_branch": c5_block_flops(S), "l2": "inputs larger than L2"},
+            "clocks": clocks,
+        })
+    if world > 1:
+        pkg.destroy_rings()
+        dist.destroy_process_group()
 
 
 def run_reference(args, world, rank, cfg, flops_layer, emit):
