@@ -98,3 +98,73 @@ def test_ring_multi_gpu():
                 assert val <= 3e-2, (rank, name, shape, val)
             else:
                 assert val <= 2e-2, (rank, name, shape, val)
+
+
+def _block_worker(rank, world, port, out_q):
+    """CFGP=2 x CP=world/2 transformer block: each rank's shard of the ring result must match the
+    same branch computed at CP=1 on one GPU."""
+    try:
+        import sys
+        from datetime import timedelta
+        from importlib import import_module
+
+        import torch.distributed as dist
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        pkg = import_module("vllm-omni-neuron_b200")
+        rope = import_module("vllm-omni-neuron_b200.rope")
+        sys.path.insert(0, os.path.dirname(__file__))
+        from test_block_gpu import make_block
+
+        cp = world // 2
+        branch, cp_rank = rank // cp, rank % cp
+        groups = tuple(tuple(range(g * cp, (g + 1) * cp)) for g in range(2))
+        H, heads = 256, 2
+        w, hidden, temb, ctx, cos, sin = make_block(1, (3, 16, 16), H, 512, 40, seed=branch)
+        S = hidden.shape[1]
+        s_loc = S // cp
+        tt = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+        wt = {k: (tt(v) if v is not None else None) for k, v in w.items()}
+        bw = pkg.prepare_block_weights(wt, heads)
+        kv = pkg.project_cross_kv(tt(ctx).to(torch.bfloat16), wt["attn2.k_proj_weight"], wt["attn2.k_proj_bias"],
+                                  wt["attn2.norm_k.weight"], wt["attn2.v_proj_weight"], wt["attn2.v_proj_bias"], heads)
+        cos_rh, sin_rh = rope.rope_rotate_half_caches(tt(cos).reshape(1, S, 1, 128), tt(sin).reshape(1, S, 1, 128))
+        cos_rh, sin_rh = cos_rh.reshape(S, 128), sin_rh.reshape(S, 128)
+        sl = slice(cp_rank * s_loc, (cp_rank + 1) * s_loc)
+        h_bf = tt(hidden).to(torch.bfloat16)
+        ring = pkg.wan_block_forward(h_bf[:, sl].contiguous(), tt(temb), (cos_rh[sl].contiguous(), sin_rh[sl].contiguous()),
+                                     kv, bw, cp_size=cp, cp_group=None, cp_replica_groups=groups)
+        full = pkg.wan_block_forward(h_bf, tt(temb), (cos_rh, sin_rh), kv, bw)
+        torch.cuda.synchronize()
+        got = ring.float().cpu().numpy().astype(np.float64)
+        ref = full[:, sl].float().cpu().numpy().astype(np.float64)
+        cos_sim = (got * ref).sum() / math.sqrt((got * got).sum() * (ref * ref).sum())
+        res = (float(cos_sim), float(np.abs(got - ref).max()))
+        pkg.destroy_rings()
+        dist.destroy_process_group()
+        out_q.put((rank, res, None))
+    except Exception:
+        out_q.put((rank, None, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs >= 4 GPUs")
+def test_block_cfg_parallel_cp():
+    world = 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_block_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, r, tb in res:
+        assert tb is None, tb
+        cos_sim, mx = r
+        assert cos_sim > 0.9999 and mx < 0.1, (rank, cos_sim, mx)
