@@ -12,6 +12,8 @@ cannot run without a Trainium toolchain):
   adaln_quant_torch.py), loaded by file path;
 * ``_eager_adaln`` (diffusion/quantization/adaln_kernels.py:51-84), loaded by file path;
 * ``WanRotaryPosEmbed`` / ``apply_rotary_emb_wan`` (diffusion/layers/rope.py), by file path;
+* ``build_fp8_dequant_mappings`` (diffusion/quantization/comfy_fp8_checkpoint.py, imported by path:
+  it needs only the standard library) and ``dequantize_to_bf16`` (dequant_loaders.py:38-52, by ``ast``);
 * ``_torch_attend`` (diffusion/models/wan2_2/wan2_2_transformer.py:640-650), ``_wan_o_proj``
   (:246-254) and ``_wan_mlp`` (:389-410), the latter two on their torch path (the NKI kernels'
   capability checks are stubbed to False),
@@ -27,6 +29,7 @@ Outputs ``*.npz`` next to this script. bf16 tensors are stored as their float32 
 from __future__ import annotations
 
 import ast
+import json
 import importlib.util
 import os
 import sys
@@ -207,6 +210,19 @@ def gen_mlp():
     np.savez_compressed(OUT / "wan_mlp.npz", **out)
 
 
+def gen_checkpoint():
+    comfy = _load_file("ref_comfy_fp8", REF / "diffusion/quantization/comfy_fp8_checkpoint.py")
+    m = comfy.build_fp8_dequant_mappings(2)
+    names = comfy.fp8_transformed_parameter_names(2)
+    (OUT / "comfy_fp8_mapping.json").write_text(json.dumps({"mappings": m, "fp8_param_names": names}, indent=0, sort_keys=True))
+    dq = _extract(REF / "diffusion/quantization/dequant_loaders.py", ["dequantize_to_bf16"], {"torch": torch})
+    rng = torch.Generator().manual_seed(20261204)
+    w = (torch.randn(48, 40, generator=rng) * 100).clamp(-448, 448).to(torch.float8_e4m3fn)
+    s = torch.tensor(0.0123, dtype=torch.float32)
+    y = dq["dequantize_to_bf16"](w, s)
+    np.savez_compressed(OUT / "fp8_dequant.npz", codes=w.view(torch.uint8).numpy(), scale=s.numpy(), y=_bf16(y))
+
+
 def main():
     if not REF.exists():
         sys.exit(f"reference checkout not found at {REF}")
@@ -222,6 +238,7 @@ def main():
     gen_rope_norm(rng)
     gen_oproj()
     gen_mlp()
+    gen_checkpoint()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
