@@ -65,3 +65,17 @@ def wan_block_ref(hidden, temb, cos, sin, cross_kv, w: dict, heads: int, eps: fl
     hidden, norm_h = adaln_modulate_oracle(y2, 1 + c_scl, c_shift, eps=eps, norm_type="layer_norm", residual=hidden)
     f = wan_mlp_ref(norm_h, w["ffn.up_weight"], w["ffn.down_weight"], w["ffn.up_bias"], w["ffn.down_bias"])
     return bf16_round(np.asarray(hidden, np.float32) + np.asarray(f, np.float32) * c_gate)
+
+
+def wan_output_head_ref(hidden, temb, table, proj_w, proj_b, eps: float = 1e-6):
+    """wan2_2_transformer.py:1824-1829: ``(norm_out(h.float()) * (1 + scale) + shift).type_as(h)`` with
+    norm_out a LayerNorm without affine parameters and ``shift, scale = (table + temb[:, None]).chunk(2)``,
+    then ``proj_out`` (``nn.Linear``, x @ W.T + b on bf16 tensors)."""
+    h = np.asarray(hidden, np.float32)
+    mods = np.asarray(table, np.float32).reshape(1, 2, -1) + np.asarray(temb, np.float32)[:, None, :]
+    shift, scale = mods[:, 0:1, :], mods[:, 1:2, :]
+    mean = h.mean(-1, keepdims=True)
+    var = ((h - mean) ** 2).mean(-1, keepdims=True)
+    y = bf16_round((h - mean) / np.sqrt(var + np.float32(eps)) * (1 + scale) + shift)
+    B, S, H = h.shape
+    return _linear(y.reshape(B * S, H), np.asarray(proj_w, np.float32).T, proj_b).reshape(B, S, -1)

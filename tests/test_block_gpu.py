@@ -64,3 +64,39 @@ def test_block_vs_oracle(pkg, dev, B, latent, H, I, L, cross_norm):
     cos_sim = (got * r).sum() / math.sqrt((got * got).sum() * (r * r).sum())
     assert cos_sim > 0.99995, cos_sim
     assert np.abs(got - r).max() <= 0.05 * max(1.0, np.abs(r).max()), np.abs(got - r).max()
+
+
+def test_two_blocks_and_output_head(pkg, dev):
+    """A 2-block DiT slice plus the output head (wan2_2_transformer.py:1814-1829) at CP=1."""
+    dit = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.dit")
+    rope = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.rope")
+    H, heads, I, L, latent = 256, 2, 512, 32, (2, 12, 16)
+    tt = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    blocks, kvs, refs = [], [], []
+    for i in range(2):
+        w, hidden0, temb, ctx, cos, sin = make_block(1, latent, H, I, L, seed=10 + i)
+        if i == 0:
+            hidden, temb0, cos0, sin0 = hidden0, temb, cos, sin
+        wt = {k: (tt(v) if v is not None else None) for k, v in w.items()}
+        blocks.append(pkg.prepare_block_weights(wt, heads))
+        kvs.append(pkg.project_cross_kv(tt(ctx).to(torch.bfloat16), wt["attn2.k_proj_weight"], wt["attn2.k_proj_bias"],
+                                        wt["attn2.norm_k.weight"], wt["attn2.v_proj_weight"], wt["attn2.v_proj_bias"], heads))
+        refs.append((w, ob.project_kv_ref(ctx, w["attn2.k_proj_weight"], w["attn2.k_proj_bias"], w["attn2.norm_k.weight"],
+                                          w["attn2.v_proj_weight"], w["attn2.v_proj_bias"], heads, 1e-6)))
+    S = hidden.shape[1]
+    cos_rh, sin_rh = rope.rope_rotate_half_caches(tt(cos0).reshape(1, S, 1, 128), tt(sin0).reshape(1, S, 1, 128))
+    rng = np.random.default_rng(3)
+    table = (rng.standard_normal((1, 2, H)) / 16).astype(np.float32)
+    temb_h = (0.1 * rng.standard_normal((1, H))).astype(np.float32)
+    proj_w = bf16_round((0.05 * rng.standard_normal((64, H))).astype(np.float32))
+    proj_b = bf16_round((0.1 * rng.standard_normal(64)).astype(np.float32))
+    x = dit.wan_blocks_forward(tt(hidden).to(torch.bfloat16), tt(temb0), (cos_rh, sin_rh), kvs, blocks)
+    out = dit.wan_output_head(x, tt(temb_h), tt(table), tt(proj_w).to(torch.bfloat16), tt(proj_b).to(torch.bfloat16))
+    torch.cuda.synchronize()
+    r = hidden
+    for w, kv in refs:
+        r = ob.wan_block_ref(r, temb0, cos0, sin0, kv, w, heads)
+    ref = ob.wan_output_head_ref(r, temb_h, table, proj_w, proj_b)
+    got = out.float().cpu().numpy().astype(np.float64)
+    cos_sim = (got * ref).sum() / math.sqrt((got * got).sum() * (ref.astype(np.float64) ** 2).sum())
+    assert out.shape == (1, S, 64) and cos_sim > 0.9999, cos_sim

@@ -158,3 +158,59 @@ def test_rank_failure_surfaces_as_error():
             p.kill()
     assert res[1].startswith("raised")
     assert res[0].startswith("error"), res[0]
+
+
+def _cp_shard_gather_worker(rank, world, port, q):
+    try:
+        import os
+        from importlib import import_module
+
+        import torch
+        import torch.distributed as dist
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        dit = import_module("vllm-omni-neuron_b200.dit")
+        g = torch.Generator().manual_seed(0)
+        hidden = torch.randn(2, 12 * world, 8, generator=g)
+        cos = torch.randn(1, 12 * world, 1, 16, generator=g)
+        sin = torch.randn(1, 12 * world, 1, 16, generator=g)
+        local, (lc, ls) = dit.cp_shard_sequence(hidden, (cos, sin), rank, world)
+        ok = torch.equal(local, hidden[:, rank * 12:(rank + 1) * 12]) and torch.equal(lc, cos[:, rank * 12:(rank + 1) * 12])
+        back = dit.cp_gather_sequence(local * 2)
+        ok = ok and torch.equal(back, hidden * 2)
+        try:
+            dit.cp_shard_sequence(hidden[:, :-1], None, rank, world)
+            ok = ok and world == 1
+        except ValueError:
+            pass
+        dist.destroy_process_group()
+        q.put((rank, ok, None))
+    except Exception:
+        import traceback
+
+        q.put((rank, False, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_cp_shard_gather_gloo(world):
+    """The DiT-level CP split / all-gather (wan2_2_transformer.py:1774-1831) on gloo ranks."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_cp_shard_gather_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, tb in res:
+        assert tb is None, tb
+        assert ok, rank

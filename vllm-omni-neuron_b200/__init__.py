@@ -19,6 +19,7 @@ from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .block import BlockWeights, prepare_block_weights, project_cross_kv, wan_block_forward
 from .build import build
+from .dit import cp_gather_sequence, cp_shard_sequence, wan_blocks_forward, wan_output_head
 from .ffn import wan_mlp
 from .leaf import wan_self_attention_fp8
 from .oproj import attn_out_norm2, o_proj_gated_residual, wan_o_proj
@@ -38,6 +39,8 @@ __all__ = [
     "attention_local",
     "attn_out_norm2",
     "build",
+    "cp_gather_sequence",
+    "cp_shard_sequence",
     "destroy_rings",
     "mx32_qkv_proj",
     "o_proj_gated_residual",
@@ -50,8 +53,10 @@ __all__ = [
     "ring_attention_const_max_fwd",
     "row_mx_qkv_proj",
     "wan_block_forward",
+    "wan_blocks_forward",
     "wan_cp_self_attention",
     "wan_mlp",
     "wan_o_proj",
+    "wan_output_head",
     "wan_self_attention_fp8",
 ]
