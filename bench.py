@@ -334,7 +334,7 @@ def main():
             lib.check(L.vomni_cm_attend(ql.data_ptr(), kl.data_ptr(), vl.data_ptr(), 1, s_loc, s_loc, 0, s_loc, HEADS, HEAD_DIM, scale,
                                         qn2.data_ptr(), km.data_ptr(), acc_o.data_ptr(), acc_l.data_ptr(), 0, None, None, st), "pass0")
             for i, (first, count) in enumerate(plan[1:], start=1):
-                fl = lib.CM_ACC_IN | ((lib.CM_FINAL | lib.CM_OUT_DMAJOR) if i == len(plan) - 1 else 0)
+                fl = lib.CM_ACC_IN | lib.CM_OVERLAP | ((lib.CM_FINAL | lib.CM_OUT_DMAJOR) if i == len(plan) - 1 else 0)
                 lib.check(L.vomni_cm_attend(ql.data_ptr(), kg.data_ptr(), vg.data_ptr(), 1, s_loc, (world - 1) * s_loc, first * s_loc,
                                             count * s_loc, HEADS, HEAD_DIM, scale, qn2.data_ptr(), km.data_ptr(), acc_o.data_ptr(),
                                             acc_l.data_ptr(), fl, o_tmp.data_ptr(), None, st), "pass")

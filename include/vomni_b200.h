@@ -79,6 +79,10 @@ VOMNI_API int vomni_memcpy_2d_async(void* dst, size_t dpitch, const void* src, s
 #define VOMNI_CM_FINAL 2      /* normalise and write bf16 out (else write the fp32 partial)   */
 #define VOMNI_CM_OUT_DMAJOR 4 /* out is [b, h, d, s] instead of [b, h, s, d]                  */
 #define VOMNI_CM_LSE 8        /* also write lse = c + ln(max(sum, 1e-37))                     */
+#define VOMNI_CM_OVERLAP 16   /* vomni_cm_attend only: the pass may start while the preceding
+                                 const-max pass on the stream still runs (programmatic dependent
+                                 launch); only its epilogue waits for that pass. q, k, v, qn2 and
+                                 kmax2 must not be written by the preceding kernel.             */
 
 /* Bytes of workspace vomni_cm_attention_local needs (norms, key max, status). */
 VOMNI_API size_t vomni_cm_workspace_bytes(int b, int s, int h, int d);

@@ -128,6 +128,57 @@ def test_ring_steps_emulated(pkg, dev, n):
     assert lib.device_status() == 0
 
 
+@pytest.mark.parametrize("s,h", [(4095, 40), (700, 6)])
+def test_overlapped_passes_equal_serial(pkg, dev, s, h):
+    """Passes launched as programmatic dependents (VOMNI_CM_OVERLAP, the ring's passes after the
+    first) give bit-identical results to serialised passes. (4095, 40) is the CP=8 shard of S=32760:
+    320 CTA pairs per pass, a partly filled last wave that the next pass overlaps."""
+    from importlib import import_module
+
+    lib = import_module("vllm-omni-neuron_b200._lib")
+    ring = import_module("vllm-omni-neuron_b200.ring")
+    L = lib.load()
+    world = 8
+    plan = ring.phase_plan(world)
+    q, k, v = _rand_qkv(1, s, h, 11, dev)
+    _, kg, vg = _rand_qkv(1, (world - 1) * s, h, 12, dev)
+    st = torch.cuda.current_stream().cuda_stream
+    qn2 = torch.empty(h, s, dtype=torch.float32, device=dev)
+    km = torch.empty(h, dtype=torch.float32, device=dev)
+    lib.check(L.vomni_cm_prologue(q.data_ptr(), k.data_ptr(), 1, s, h, 128, qn2.data_ptr(), km.data_ptr(), st), "prologue")
+    qn2_g = torch.empty(h, (world - 1) * s, dtype=torch.float32, device=dev)
+    km_g = torch.empty(h, dtype=torch.float32, device=dev)
+    lib.check(L.vomni_cm_prologue(kg.data_ptr(), kg.data_ptr(), 1, (world - 1) * s, h, 128, qn2_g.data_ptr(),
+                                  km_g.data_ptr(), st), "prologue")
+    km = torch.maximum(km, km_g)
+    scale = 1 / math.sqrt(128)
+    outs = []
+    for overlap in (0, lib.CM_OVERLAP):
+        acc_o = torch.empty(h, s, 128, dtype=torch.float32, device=dev)
+        acc_l = torch.empty(h, s, dtype=torch.float32, device=dev)
+        out = torch.empty(1, h, 128, s, dtype=torch.bfloat16, device=dev)
+        lse = torch.zeros(1, h, 128, (s + 127) // 128, dtype=torch.float32, device=dev)  # pad rows stay 0
+        lib.check(L.vomni_cm_attend(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, s, s, 0, s, h, 128, scale, qn2.data_ptr(),
+                                    km.data_ptr(), acc_o.data_ptr(), acc_l.data_ptr(), 0, None, None, st), "pass0")
+        for i, (first, count) in enumerate(plan[1:], start=1):
+            fl = lib.CM_ACC_IN | overlap
+            if i == len(plan) - 1:
+                fl |= lib.CM_FINAL | lib.CM_OUT_DMAJOR | lib.CM_LSE
+            lib.check(L.vomni_cm_attend(q.data_ptr(), kg.data_ptr(), vg.data_ptr(), 1, s, (world - 1) * s, first * s,
+                                        count * s, h, 128, scale, qn2.data_ptr(), km.data_ptr(), acc_o.data_ptr(),
+                                        acc_l.data_ptr(), fl, out.data_ptr(), lse.data_ptr(), st), "pass")
+        outs.append((out, lse))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
+    assert lib.device_status() == 0
+    if s <= 1024:
+        kf = torch.cat([k, kg], dim=1)
+        vf = torch.cat([v, vg], dim=1)
+        ref = oat.const_max_ring_attention([_f32(q)], [_f32(kf)], [_f32(vf)])[0]
+        _cmp(_f32(outs[1][0]).transpose(0, 1, 3, 2), ref, "overlapped passes vs oracle")
+
+
 def test_key_subrange_masking(pkg, dev):
     """A pass over keys [k_start, k_start+n_keys) of a longer K/V must ignore the keys outside."""
     from importlib import import_module

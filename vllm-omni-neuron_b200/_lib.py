@@ -86,6 +86,7 @@ CM_ACC_IN = 1
 CM_FINAL = 2
 CM_OUT_DMAJOR = 4
 CM_LSE = 8
+CM_OVERLAP = 16
 
 _lib = None
 _lock = threading.Lock()

@@ -84,6 +84,19 @@ static int get_encoder() {
   return VOMNI_OK;
 }
 
+StreamWriteValue32Fn stream_write_value32() {
+  static StreamWriteValue32Fn fn_ptr = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuStreamWriteValue32", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn_ptr = reinterpret_cast<StreamWriteValue32Fn>(fn);
+  });
+  return fn_ptr;
+}
+
 int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
                       uint32_t box1, uint64_t row_pitch_elems) {
   int rc = get_encoder();

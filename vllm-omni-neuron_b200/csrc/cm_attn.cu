@@ -70,6 +70,8 @@ struct Params {
   float* lse;          // [b*h, 128, ceil(s_q/128)]
   int flags;
   int* status;
+  const unsigned* ready;  // if set: K/V of this pass are valid once *ready reaches ready_epoch
+  unsigned ready_epoch;
 };
 
 // S = Q_t K^T: 8 MMAs of K=16 over the two 64-wide swizzled halves (K-major SW128: +32 B per step).
@@ -253,6 +255,9 @@ VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort
   // ---------------------------------------------------------- epilogue
   if (ok && mbar_wait(&bars[O_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) {
     tc_fence_after();
+    // A pass launched as a programmatic dependent of the previous pass reads and writes acc / out
+    // only from here on, after that pass has completed.
+    pdl_wait();
     const bool acc_in = p.flags & VOMNI_CM_ACC_IN;
     const bool final_pass = p.flags & VOMNI_CM_FINAL;
     float l = rowsum;
@@ -320,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
   const int q0 = blockIdx.x * kTile * kQT;
   const int bh = blockIdx.y;
   const int b = bh / p.heads;
@@ -367,7 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(&tmQ, &bars[Q_FULL], sQ + t * kTileBytes, x0, q0 + t * kTile, b);
         tma_load_3d(&tmQ, &bars[Q_FULL], sQ + t * kTileBytes + kHalfBytes, x0 + 64, q0 + t * kTile, b);
       }
-      for (int j = 0; j < n_tiles; ++j) {
+      const bool kv_ready = !p.ready || ready_wait(p.ready, p.ready_epoch, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 10);
+      for (int j = 0; kv_ready && j < n_tiles; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         const int k_row = p.k_start + j * kTile;
@@ -441,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tbase, 512);
   }
+  pdl_wait();  // this grid completes only after the pass it overlapped (also on an abort path)
 }
 
 // ---------------------------------------------------------------- CTA-pair attention
@@ -491,6 +499,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int q_base = (blockIdx.x >> 1) * (2 * kTile * kQT) + static_cast<int>(rank) * kTile;  // this CTA's tile-0 rows
@@ -542,7 +551,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_load_3d_pair(&tmQ, lead_bars + Q_FULL * 8, sQ + t * kTileBytes, x0, qr, b);
         tma_load_3d_pair(&tmQ, lead_bars + Q_FULL * 8, sQ + t * kTileBytes + kHalfBytes, x0 + 64, qr, b);
       }
-      for (int j = 0; j < n_tiles; ++j) {
+      const bool kv_ready = !p.ready || ready_wait(p.ready, p.ready_epoch, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x20);
+      for (int j = 0; kv_ready && j < n_tiles; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         const int k_row = p.k_start + j * kTile;
@@ -605,6 +615,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tbase, 512);
   }
+  pdl_wait();  // this grid completes only after the pass it overlapped (also on an abort path)
 }
 
 // ---------------------------------------------------------------- prologue norms
@@ -718,10 +729,19 @@ extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void*
                                        int k_start, int n_keys, int h, int d, long long q_stride, long long kv_stride,
                                        float softmax_scale, const float* qn2, const float* kmax2, float* acc_o,
                                        float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream) {
+  return vomni::cm_attend_gated(q, k, v, b, s_q, s_kv, k_start, n_keys, h, d, q_stride, kv_stride, softmax_scale, qn2,
+                                kmax2, acc_o, acc_l, flags, out, lse, nullptr, 0u, stream);
+}
+
+int vomni::cm_attend_gated(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start,
+                           int n_keys, int h, int d, long long q_stride, long long kv_stride, float softmax_scale,
+                           const float* qn2, const float* kmax2, float* acc_o, float* acc_l, int flags, void* out,
+                           float* lse, const unsigned* ready, unsigned ready_epoch, vomni_stream_t stream) {
   if (!q || !k || !v || !qn2 || !kmax2) return VOMNI_EINVAL;
   if (d != cm::kD || b <= 0 || s_q <= 0 || h <= 0 || n_keys <= 0 || k_start < 0 || k_start + n_keys > s_kv)
     return VOMNI_EBADSHAPE;
-  if (flags & ~(VOMNI_CM_ACC_IN | VOMNI_CM_FINAL | VOMNI_CM_OUT_DMAJOR | VOMNI_CM_LSE)) return VOMNI_EINVAL;
+  if (flags & ~(VOMNI_CM_ACC_IN | VOMNI_CM_FINAL | VOMNI_CM_OUT_DMAJOR | VOMNI_CM_LSE | VOMNI_CM_OVERLAP))
+    return VOMNI_EINVAL;
   const bool final_pass = flags & VOMNI_CM_FINAL;
   if (final_pass && !out) return VOMNI_EINVAL;
   if ((flags & VOMNI_CM_LSE) && !lse) return VOMNI_EINVAL;
@@ -760,6 +780,8 @@ extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void*
   p.lse = lse;
   p.flags = flags;
   p.status = device_status_ptr();
+  p.ready = ready;
+  p.ready_epoch = ready_epoch;
 
   // Tuning knobs (read once): VOMNI_CM_POLY = share of exponentials on the FMA pipe as 1/N
   // (0 = none), VOMNI_CM_SPLIT = 1 to publish P in two key halves, 0 for whole tiles,
@@ -780,9 +802,17 @@ extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void*
     auto pk = poly == 8 ? cm::cm_attend_pair_kernel<8> : cm::cm_attend_pair_kernel<0>;
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kPairSmemBytes));
     const int pairs = (s_q + 4 * cm::kTile - 1) / (4 * cm::kTile);
-    dim3 grid(2 * pairs, b * h);
-    pk<<<grid, cm::kThreads, cm::kPairSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk2, tv, p);
-    VOMNI_CUDA_TRY(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, b * h);
+    cfg.blockDim = dim3(cm::kThreads);
+    cfg.dynamicSmemBytes = cm::kPairSmemBytes;
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (flags & VOMNI_CM_OVERLAP) ? 1 : 0;
+    VOMNI_CUDA_TRY(cudaLaunchKernelEx(&cfg, pk, tq, tk2, tv, p));
     return VOMNI_OK;
   }
   auto kern = cm::cm_attend_kernel<0, false>;
@@ -791,9 +821,17 @@ extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void*
   else if (poly == 8) kern = split ? cm::cm_attend_kernel<8, true> : cm::cm_attend_kernel<8, false>;
   else kern = split ? cm::cm_attend_kernel<0, true> : cm::cm_attend_kernel<0, false>;
   VOMNI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kSmemBytes));
-  dim3 grid((s_q + cm::kTile * cm::kQT - 1) / (cm::kTile * cm::kQT), b * h);
-  kern<<<grid, cm::kThreads, cm::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  VOMNI_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((s_q + cm::kTile * cm::kQT - 1) / (cm::kTile * cm::kQT), b * h);
+  cfg.blockDim = dim3(cm::kThreads);
+  cfg.dynamicSmemBytes = cm::kSmemBytes;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & VOMNI_CM_OVERLAP) ? 1 : 0;
+  VOMNI_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p));
   return VOMNI_OK;
 }
 

@@ -33,6 +33,11 @@ VOMNI_DEV uint64_t globaltimer() {
 VOMNI_DEV void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
+// Programmatic dependent launch: let the next kernel on the stream start its CTAs once every CTA of
+// this grid has issued the trigger; the dependent's wait blocks until this grid has completed and its
+// memory is visible (a no-op when the kernel was not launched as a dependent).
+VOMNI_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+VOMNI_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 VOMNI_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 VOMNI_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
@@ -79,6 +84,29 @@ VOMNI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, in
       if (status) atomicCAS(status, 0, code);
       return false;
     }
+  }
+}
+
+// Bounded wait until a 32-bit ready word, written by a stream memory operation after copies on
+// another stream, reaches `target` (wrap-safe). Acquire, then order the async proxy (TMA reads of
+// the copied data) after it.
+VOMNI_DEV bool ready_wait(const unsigned* word, unsigned target, volatile int* abort, int* status, int code,
+                          uint64_t budget_ns = kWaitBudgetNs) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(word) : "memory");
+    if (static_cast<int>(v - target) >= 0) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      return true;
+    }
+    if (*abort) return false;
+    if (globaltimer() - t0 > budget_ns) {
+      *abort = 1;
+      if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+    __nanosleep(500);
   }
 }
 

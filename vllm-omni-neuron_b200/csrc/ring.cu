@@ -10,8 +10,12 @@
 // becomes direct pulls: step s copies block (r - s) mod N straight from its owner's registered send
 // buffer into a local gather buffer, on a copy-engine stream (cudaMemcpyAsync between IPC-mapped
 // device memory; no SMs, no TMA on peer memory, no multicast). The attention runs as a few passes
-// over ranges of arrived blocks (local block first, then ranges of 1, 2, 4, ... blocks), each gated
-// on the copy events of its blocks and accumulating into an fp32 partial; the last pass normalises.
+// over ranges of arrived blocks (local block first, then ranges of 1, 2, 4, ... blocks), accumulating
+// into an fp32 partial; the last pass normalises. After a block's copies the copy stream posts a
+// per-step ready word (cuStreamWriteValue32, executed by the GPU front end, not by a kernel); each
+// pass waits for its last block's word inside the kernel (bounded), before its first K/V load, so
+// no stream-level wait separates consecutive passes and a pass starts as a programmatic dependent
+// of the previous one, filling the SMs its last wave leaves idle.
 //
 // Ordering guarantees (no device-side cross-GPU waits anywhere):
 //  * peers' send buffers are complete before this rank copies them: each rank writes its send
@@ -19,12 +23,14 @@
 //    every peer reached it, i.e. finished its earlier stream work;
 //  * send buffers are double-buffered by call parity: a rank rewrites send[p] two calls later, after
 //    the intervening call's all_reduce, by which time every peer's copies of send[p] have completed
-//    (each peer's passes wait on its copy events before that peer can enter the next all_reduce).
+//    (each rank's stream joins its copy stream after the last pass, before it can enter the next
+//    all_reduce).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -84,6 +90,7 @@ struct vomni_ring {
   cudaEvent_t ev_ready = nullptr;  // recorded on the caller stream after the all_reduce
   std::vector<cudaEvent_t> ev_block;  // copy of ring step s done
   cudaEvent_t ev_copies_done = nullptr;
+  unsigned* ready = nullptr;  // [world] device words: ready[s] = call number once step s's block landed
   // Registered send buffer: [parity 2][K|V 2][b, s_max, h, d] bf16 (one allocation, IPC-exported).
   void* send = nullptr;
   size_t block_bytes = 0;  // one K or V block at s_max
@@ -117,6 +124,7 @@ void ring_free(vomni_ring* R) {
   if (R->kmax2) cudaFree(R->kmax2);
   if (R->acc_o) cudaFree(R->acc_o);
   if (R->acc_l) cudaFree(R->acc_l);
+  if (R->ready) cudaFree(R->ready);
   for (cudaEvent_t e : R->ev_block) cudaEventDestroy(e);
   if (R->ev_ready) cudaEventDestroy(R->ev_ready);
   if (R->ev_copies_done) cudaEventDestroy(R->ev_copies_done);
@@ -134,12 +142,24 @@ void ring_free(vomni_ring* R) {
 extern "C" int vomni_ring_phase_plan(int world, int* first, int* count, int max_phases) {
   // Pass 0 is the local block; passes 1.. cover gather slots [first, first+count) with counts
   // 1, 2, 4, ... (the last pass takes the remainder). Returns the number of passes.
+  // VOMNI_RING_PLAN="c1,c2,..." (tuning knob) replaces the doubling sizes; the last listed size
+  // repeats until all world - 1 slots are covered.
   if (world < 1 || !first || !count || max_phases < 1) return -VOMNI_EINVAL;
   int n = 0;
   first[n] = -1;
   count[n] = 1;
   ++n;
-  int slot = 0, size = 1;
+  int sizes[16], n_sizes = 0;
+  if (const char* e = getenv("VOMNI_RING_PLAN")) {
+    while (*e && n_sizes < 16) {
+      const int c = atoi(e);
+      if (c < 1) return -VOMNI_EINVAL;
+      sizes[n_sizes++] = c;
+      while (*e && *e != ',') ++e;
+      if (*e == ',') ++e;
+    }
+  }
+  int slot = 0, size = n_sizes ? sizes[0] : 1, k = 0;
   while (slot < world - 1) {
     if (n >= max_phases) return -VOMNI_EINVAL;
     const int c = (slot + size > world - 1) ? world - 1 - slot : size;
@@ -147,7 +167,10 @@ extern "C" int vomni_ring_phase_plan(int world, int* first, int* count, int max_
     count[n] = c;
     ++n;
     slot += c;
-    size *= 2;
+    if (n_sizes)
+      size = sizes[++k < n_sizes ? k : n_sizes - 1];
+    else
+      size *= 2;
   }
   return n;
 }
@@ -224,6 +247,8 @@ extern "C" int vomni_ring_create(vomni_ring** out, int rank, int world, const vo
     RING_CUDA(cudaMalloc(&R->gather_v, R->block_bytes * (world - 1)));
     RING_CUDA(cudaMalloc(&R->acc_o, static_cast<size_t>(b) * h * s_max * d * sizeof(float)));
     RING_CUDA(cudaMalloc(&R->acc_l, static_cast<size_t>(b) * h * s_max * sizeof(float)));
+    RING_CUDA(cudaMalloc(&R->ready, sizeof(unsigned) * world));
+    RING_CUDA(cudaMemsetAsync(R->ready, 0, sizeof(unsigned) * world, R->copy_stream));  // synchronised below
     // Exchange IPC handles of the send buffers with one all_gather (handles staged through device memory).
     cudaIpcMemHandle_t mine;
     RING_CUDA(cudaIpcGetMemHandle(&mine, R->send));
@@ -319,6 +344,8 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
 
   const int parity = static_cast<int>(R->calls & 1);
   ++R->calls;
+  const unsigned epoch = static_cast<unsigned>(R->calls);
+  const StreamWriteValue32Fn write_value = stream_write_value32();
   // 1. publish this rank's K/V block in its registered send buffer (b blocks of s_loc tokens; the
   //    buffer keeps an s_max stride per batch so peers address it with the creation-time geometry).
   uint8_t* my_send = static_cast<uint8_t*>(R->send) + static_cast<size_t>(parity) * 2 * R->block_bytes;
@@ -353,7 +380,11 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
       VOMNI_CUDA_TRY(cudaMemcpyAsync(gv, ps + R->block_bytes + bi * bstride, blk, cudaMemcpyDeviceToDevice, R->copy_stream));
     }
     VOMNI_CUDA_TRY(cudaEventRecord(R->ev_block[s], R->copy_stream));
+    if (write_value && write_value(reinterpret_cast<CUstream>(R->copy_stream),
+                                   reinterpret_cast<CUdeviceptr>(R->ready + s), epoch, 0) != CUDA_SUCCESS)
+      return VOMNI_ECUDA;
   }
+  VOMNI_CUDA_TRY(cudaEventRecord(R->ev_copies_done, R->copy_stream));
   // 5. passes: local block, then ranges of arrived blocks; fp32 partial, normalise on the last
   int first[64], count[64];
   const int np = vomni_ring_phase_plan(N, first, count, 64);
@@ -364,12 +395,22 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
   const int s_kv = (N - 1) * s_loc;
   for (int p = 1; p < np; ++p) {
     const int last_step = first[p] + count[p];  // ring step of the last block in this pass
-    VOMNI_CUDA_TRY(cudaStreamWaitEvent(st, R->ev_block[last_step], 0));
-    const int fl = VOMNI_CM_ACC_IN | (p == np - 1 ? (VOMNI_CM_FINAL | flags) : 0);
-    rc = vomni_cm_attend_strided(q, R->gather_k, R->gather_v, b, s_loc, s_kv, first[p] * s_loc, count[p] * s_loc, h, d,
-                                 q_stride, 0, softmax_scale, R->qn2, R->kmax2, R->acc_o, R->acc_l, fl, out, lse, stream);
+    int fl = VOMNI_CM_ACC_IN | (p == np - 1 ? (VOMNI_CM_FINAL | flags) : 0);
+    if (write_value) {
+      // In-kernel gate on the block's ready word; the pass overlaps the previous pass's last wave
+      // and only its epilogue (the accumulator read-modify-write) waits for that pass.
+      fl |= VOMNI_CM_OVERLAP;
+    } else {
+      VOMNI_CUDA_TRY(cudaStreamWaitEvent(st, R->ev_block[last_step], 0));
+    }
+    rc = cm_attend_gated(q, R->gather_k, R->gather_v, b, s_loc, s_kv, first[p] * s_loc, count[p] * s_loc, h, d,
+                         q_stride, 0, softmax_scale, R->qn2, R->kmax2, R->acc_o, R->acc_l, fl, out, lse,
+                         write_value ? R->ready + last_step : nullptr, epoch, stream);
     if (rc) return rc;
   }
+  // Join the copy stream: this rank's copies of its peers' send buffers are complete before any later
+  // work on the caller stream (the next call's all_reduce included).
+  VOMNI_CUDA_TRY(cudaStreamWaitEvent(st, R->ev_copies_done, 0));
   return VOMNI_OK;
 }
 
