@@ -58,6 +58,12 @@ VOMNI_API int vomni_device_status(int* code, int clear);
  * word reads VOMNI_DEV_TIMEOUT_BASE + 0x7F and *result_host = 0 (1 would mean the wait
  * completed). Synchronises `stream`. */
 VOMNI_API int vomni_selftest_bounded_wait(unsigned budget_us, int* result_host, vomni_stream_t stream);
+/* Same for the ring's block-ready gate: one CTA waits (budget_us, <= 2 s) for a device word to
+ * reach 1. post = 1: the word is first posted on `stream` with the stream memory operation the ring
+ * uses (cuStreamWriteValue32), the wait completes, *result_host = 1 and the status stays 0.
+ * post = 0: nothing posts it, the wait gives up, *result_host = 0 and the status word reads
+ * VOMNI_DEV_TIMEOUT_BASE + 0x7E. Synchronises `stream`. */
+VOMNI_API int vomni_selftest_ready_wait(unsigned budget_us, int post, int* result_host, vomni_stream_t stream);
 /* Stream-ordered 2-D copy (height rows of width bytes; pitches in bytes) between any two of host
  * (pinned) and device memory: the host-resident attention entry streams head groups with it.
  * No counterpart in the reference (its inputs are always device-resident). */

@@ -211,6 +211,39 @@ extern "C" int vomni_selftest_bounded_wait(unsigned budget_us, int* result_host,
   return VOMNI_OK;
 }
 
+__global__ void selftest_ready_kernel(const unsigned* word, uint64_t budget_ns, int* status, int* result) {
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) abort_flag = 0;
+  __syncthreads();
+  if (threadIdx.x == 0)
+    *result = vomni::ready_wait(word, 1u, &abort_flag, status, VOMNI_DEV_TIMEOUT_BASE + 0x7E, budget_ns) ? 1 : 0;
+}
+
+extern "C" int vomni_selftest_ready_wait(unsigned budget_us, int post, int* result_host, vomni_stream_t stream) {
+  if (!result_host || budget_us == 0 || budget_us > 2000000u || (post != 0 && post != 1)) return VOMNI_EINVAL;
+  int* st = vomni::device_status_ptr();
+  if (!st) return VOMNI_ECUDA;
+  const vomni::StreamWriteValue32Fn write_value = vomni::stream_write_value32();
+  if (post && !write_value) return VOMNI_ENOTSUP;
+  int* d = nullptr;
+  VOMNI_CUDA_TRY(cudaMalloc(&d, 2 * sizeof(int)));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  unsigned* word = reinterpret_cast<unsigned*>(d + 1);
+  cudaError_t e = cudaMemsetAsync(d, 0, 2 * sizeof(int), s);
+  if (e == cudaSuccess && post &&
+      write_value(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(word), 1u, 0) != CUDA_SUCCESS)
+    e = cudaErrorUnknown;
+  if (e == cudaSuccess) {
+    selftest_ready_kernel<<<1, 32, 0, s>>>(word, static_cast<uint64_t>(budget_us) * 1000ull, st, d);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(result_host, d, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(d);
+  VOMNI_CUDA_TRY(e);
+  return VOMNI_OK;
+}
+
 extern "C" int vomni_memcpy_2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
                                      size_t height, vomni_stream_t stream) {
   if (!dst || !src) return VOMNI_EINVAL;
