@@ -214,6 +214,17 @@ VOMNI_API int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, c
 VOMNI_API int vomni_linear_sumsq(const void* x, long long m, int k, const void* w, const void* bias, int n,
                                  float* sumsq, int n_norm_heads, void* out, vomni_stream_t stream);
 
+/* ------------------------------------------------------------------ CFG-parallel combine
+ * The combine of _cfg_gather_combine (diffusion/distributed/cfg_parallel.py:48-71) after the CFG
+ * group's all_gather: out[i] = negative[i] + scale * (positive[i] - negative[i]) over n elements,
+ * with torch eager rounding: for dtype VOMNI_CFG_BF16 every step is computed in fp32 and rounded to
+ * bf16 (difference, product, sum), for VOMNI_CFG_F32 in fp32 without contraction. out may alias
+ * positive or negative. */
+#define VOMNI_CFG_F32 0
+#define VOMNI_CFG_BF16 1
+VOMNI_API int vomni_cfg_combine(const void* positive, const void* negative, void* out, long long n, int dtype,
+                                float scale, vomni_stream_t stream);
+
 /* ------------------------------------------------------------------ context-parallel ring
  * Replaces the ring driver of ring_attention_const_max_fwd(num_workers = N > 1)
  * (ring_attention_const_max_fwd.py:1196-1205 all_reduce(max) of the key norm, :1287-1398 K/V

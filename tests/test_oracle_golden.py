@@ -171,3 +171,23 @@ def test_mlp_oracle_vs_reference_golden(golden):
         step = np.exp2(np.floor(np.log2(np.maximum(np.maximum(np.abs(ref), np.abs(y)), 2.0 ** -100))) - 7)
         assert (np.abs(y - ref) <= 2 * step * 1.0001 + 2e-3).all(), tag
         assert (y == ref).mean() > 0.999, tag
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("scale", [5.0, 3.5, 1.0, 7.3])
+def test_cfg_combine_matches_torch_eager(dtype, scale):
+    """The restated CFG combine equals the reference's own expression
+    (``negative + true_cfg_scale * (positive - negative)``, cfg_parallel.py:71) run by torch eager."""
+    import torch
+
+    from oracle import cfg as ocfg
+
+    g = torch.Generator().manual_seed(7)
+    td = torch.bfloat16 if dtype == "bf16" else torch.float32
+    # latent-shaped branch outputs [B, C, T, H, W] plus a ragged flat tail
+    for shape in ((1, 16, 3, 12, 20), (1001,)):
+        pos = torch.randn(shape, generator=g).to(td)
+        neg = (torch.randn(shape, generator=g) * 0.7).to(td)
+        ref = (neg + scale * (pos - neg)).float().numpy()
+        got = ocfg.cfg_gather_combine_ref([pos.float().numpy(), neg.float().numpy()], scale, dtype == "bf16")
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))

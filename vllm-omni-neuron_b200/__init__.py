@@ -10,6 +10,7 @@ Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call AP
   with the block's gated residual + norm2 adaLN
 * :func:`wan_mlp` — the block's FFN (GELU-tanh MLP)
 * :func:`wan_block_forward` — a whole transformer block (self-attn + cross-attn + FFN, bf16 leaves)
+* :func:`cfg_gather_combine` — the CFG-parallel gather + combine of the two branch outputs
 
 Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``) built by
 :func:`build`.
@@ -19,6 +20,7 @@ from .adaln import adaln_modulate
 from .attention import attention_local, ring_attention_const_max_fwd, wan_cp_self_attention
 from .block import BlockWeights, prepare_block_weights, project_cross_kv, wan_block_forward
 from .build import build
+from .cfg import cfg_combine, cfg_gather_combine
 from .dit import cp_gather_sequence, cp_shard_sequence, wan_blocks_forward, wan_output_head
 from .ffn import wan_mlp
 from .leaf import wan_self_attention_fp8
@@ -39,6 +41,8 @@ __all__ = [
     "attention_local",
     "attn_out_norm2",
     "build",
+    "cfg_combine",
+    "cfg_gather_combine",
     "cp_gather_sequence",
     "cp_shard_sequence",
     "destroy_rings",
