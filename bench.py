@@ -40,6 +40,7 @@ CONFIGS = {
     "c4": dict(S=75600, latent=(21, 90, 160), desc="C4: Wan2.2-A14B 720x1280x81 self-attention, S=75600 (21x45x80 tokens), H=40 D=128"),
     "c5": dict(S=32760, latent=(21, 60, 104), desc="C5: CFG-parallel Wan2.2-A14B transformer block (self-attn + cross-attn to 512 text tokens + FFN 5120-13824-5120 GELU-tanh), bf16, B=2 (cond/uncond) split CFGP=2 x CP=N/2 (N=1: one branch, CP=1)"),
     "ffn": dict(S=32760, latent=None, desc="Wan FFN of one block on the C2 token count: GELU_tanh(x @ Wu + bu) @ Wd + bd, x [32760, 5120], Wu [5120, 13824], Wd [13824, 5120], bf16"),
+    "ffn_fp8": dict(S=32760, latent=None, desc="Wan FFN FP8 leaf (row_mx_mlp, ROW_MX) on the C2 token count: ROW e4m3 x [32760, 5120] -> up GEMM + GELU-tanh + MX-32 quant of the [32760, 13824] intermediate -> block-scaled down GEMM + per-channel scale + bias + gated residual"),
     "oproj": dict(S=32760, latent=None, desc="Output projection of one C2 self-attention layer (d-major [1,40,128,32760] @ [5120,5120] + bias) with the norm2 gated residual and adaLN (LayerNorm + FP8 row quant)"),
 }
 METRIC = "ring-attn TFLOP/s at S=32760 (one Wan2.2-A14B self-attention layer), CP=N"
@@ -216,6 +217,8 @@ def main():
         return run_oproj(args, emit)
     if args.config == "ffn":
         return run_ffn(args, emit)
+    if args.config == "ffn_fp8":
+        return run_ffn_fp8(args, emit)
     if args.config == "c5":
         return run_c5(args, world, rank, local_rank, emit)
 
@@ -668,6 +671,67 @@ def run_ffn(args, emit):
         "config": {"workload": CONFIGS["ffn"]["desc"], "T": T, "H": H, "I": I, "l2": "flushed (256 MB write) before each call"},
         "roofline": {"bound": "tensor", "achieved": round(flops / t / 1e9, 1), "peak": bf16, "unit": "TFLOP/s",
                      "frac": round(flops / t / 1e9 / bf16, 4), "peak_source": "measured (bf16_tflops burst)"},
+        "clocks": clocks, "gpu_launches": 2 * n,
+    })
+
+
+def run_ffn_fp8(args, emit):
+    """The FFN's FP8 leaf (row_mx_mlp): e4m3 ROW up GEMM with the GELU + MX-32 epilogue, block-scaled
+    MX down GEMM with the closing gated residual."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module(PKG)
+    pkg.build()
+    lib = importlib.import_module(PKG + "._lib")
+    T, H, I = (args.tokens or 32760), HIDDEN, 13824
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(T, H, generator=g, device=dev)
+    rs = torch.clamp(x.abs().amax(1) / 448.0, min=1e-6)
+    codes = (x / rs[:, None]).to(torch.float8_e4m3fn)
+    del x
+    uc, us, dc, ds = pkg.quantize_mlp_weights_row_mx(torch.randn(H, I, generator=g, device=dev) * 0.02,
+                                                     torch.randn(I, H, generator=g, device=dev) * 0.02)
+    bu = (torch.randn(I, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    bd = (torch.randn(H, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    res = torch.randn(1, T, H, generator=g, device=dev).to(torch.bfloat16)
+    gate = torch.randn(1, 1, H, generator=g, device=dev) * 0.1
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        return pkg.row_mx_mlp((codes, rs), uc, dc, us, ds, bu, bd, residual=res, gate=gate)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    n = max(args.steps, 5)
+    sampler = ClockSampler(0)
+    sampler.start()
+    ts = []
+    for _ in range(n):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    clocks = sampler.stop()
+    assert lib.device_status() == 0
+    t = statistics.median(ts)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    fp8 = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    flops = 4.0 * T * H * I
+    emit({
+        "metric": "Wan FFN FP8 leaf TFLOP/s (row_mx_mlp, one block, C2 token count)", "value": round(flops / t / 1e9, 1),
+        "unit": "TFLOP/s", "ms_per_step": round(t, 4), "higher_is_better": True, "n_gpus": 1, "steps": n,
+        "warmup": args.warmup, "dtype": "e4m3 (fp32 accumulate, MX-32 intermediate)", "data": "synthetic",
+        "config": {"workload": CONFIGS["ffn_fp8"]["desc"], "T": T, "H": H, "I": I,
+                   "l2": "flushed (256 MB write) before each call"},
+        "roofline": {"bound": "tensor", "achieved": round(flops / t / 1e9, 1), "peak": fp8, "unit": "TFLOP/s",
+                     "frac": round(flops / t / 1e9 / fp8, 4),
+                     "peak_source": "2 x measured bf16_tflops burst (dense fp8 rate = 2 x bf16 on B200)"},
         "clocks": clocks, "gpu_launches": 2 * n,
     })
 

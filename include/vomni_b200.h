@@ -207,6 +207,29 @@ VOMNI_API int vomni_ffn_gemm(const void* x, long long m, int k, const void* w, c
                              const void* residual, const float* gate, long long gate_rows, void* out,
                              vomni_stream_t stream);
 
+/* ROW_MX MLP (FP8 FFN leaf): row_mx_mlp (diffusion/quantization/row_mx_kernels.py:141-198), the
+ * nkilib MLP in ROW_MX / CTE mode whose arithmetic kernels/nkilib/core/mlp/mlp_torch.py:401-600 states.
+ * Up: x_codes [t, h] e4m3 with row_scale [t] fp32 (the ROW-quantised adaLN output, codes split from
+ * the packed [t, h+4] rows), w_codes [i, h] e4m3 (W_up^T, K-major) with chan_scale [i] fp32 and bias
+ * [i] bf16 (NULL = 0): v = gelu_tanh(acc * row_scale * chan_scale + bias) in fp32, MX-32 quantised
+ * along i (UE8M0 scale = max biased exponent of 32 values - 7, clip [0, 255]; codes e4m3fn,
+ * saturating at 448; _mx_quantize, mlp_torch.py:252-271) into inter_codes [t, i] and
+ * inter_sf_packed (vomni_mx_packed_scales_bytes(t, i) bytes, the tcgen05 atom layout of
+ * vomni_mx_pack_scales). h % 128 == 0, i % 256 == 0. */
+VOMNI_API int vomni_ffn_fp8_up(const void* x_codes, const float* row_scale, const void* w_codes,
+                               const float* chan_scale, const void* bias, int t, int h, int i, void* inter_codes,
+                               void* inter_sf_packed, vomni_stream_t stream);
+/* Down: out [t, h] bf16 = bf16(acc * chan_scale + bias) with acc the block-scaled product of the
+ * intermediate (inter_codes, inter_sf_packed) and w_codes [h, i] e4m3 (W_down^T, K-major) whose
+ * packed block scales w_sf_packed are all 127 (identity; vomni_mx_packed_scales_bytes(h, i) bytes);
+ * chan_scale [h] fp32, bias [h] bf16 (NULL = 0). With a residual [t, h] bf16 the kernel writes the
+ * block's closing gated residual bf16(residual + gate * y) instead (wan2_2_transformer.py:1510-1512;
+ * gate fp32 [t / gate_rows, h], NULL = 1). i % 128 == 0, h % 256 == 0. */
+VOMNI_API int vomni_ffn_fp8_down(const void* inter_codes, const void* inter_sf_packed, const void* w_codes,
+                                 const void* w_sf_packed, const float* chan_scale, const void* bias, int t, int i,
+                                 int h, const void* residual, const float* gate, long long gate_rows, void* out,
+                                 vomni_stream_t stream);
+
 /* bf16 projection for the across-heads RMS norm that follows (the bf16 self-attention leaf's
  * qkv_proj + norm_q/norm_k, wan2_2_transformer.py:1097-1109, and the cross-attention's q/k
  * projections, :1232-1248): out [m, n] = bf16(bf16(x @ w) + bias) and sumsq [m, n_norm_heads] = per

@@ -6,12 +6,34 @@
     out = bf16(bf16(g @ Wd) + bd)
 
 Pinned by ``tests/golden/wan_mlp.npz`` (outputs of ``_wan_mlp`` itself).
+
+``wan_mlp_row_mx_ref`` restates the FP8 leaf ``row_mx_mlp``
+(vllm_omni_neuron/diffusion/quantization/row_mx_kernels.py:141-198), the nkilib MLP kernel in ROW_MX
+CTE mode, following its PyTorch reference ``_mlp_ref_standard``
+(vllm_omni_neuron/kernels/nkilib/core/mlp/mlp_torch.py:401-600) with ``skip_gate_proj=True`` and
+``GELU_Tanh_Approx``:
+
+    up    = (Xq * row_scale) @ (Wu_q * wu_scale) + bu       (fp32; :470-486 pre-quantised ROW input,
+                                                             :491-497 per-channel weight scales)
+    inter = gelu_tanh(up)                                     (:580-582)
+    inter_q, s = _mx_quantize(inter)                          (:587-589, 252-271: one shared
+             exponent per 32 contiguous values = max biased fp32 exponent - 7, codes
+             clip(inter / 2^(e-127), +-448) rounded to e4m3fn, :599)
+    out   = (inter_q * s) @ (Wd_q * wd_scale) + bd           (:593-596), returned as bf16 (the
+                                                             kernel's ``output_dtype="bfloat16"``)
+
+Partly pinned: the MX block size is ``_q_height * _q_width`` from
+``nkilib.core.mlp.mlp_tkg.projection_mx_constants``, which is not in the reference tree; 32 (the MX
+block of the rest of the reference, ``adaln_quant_torch.py:151-175``) is assumed, and the
+exponent clip to [0, 255] (a UE8M0 byte) only differs from the unclipped reference for blocks whose
+largest magnitude is below 2^-120.
 """
 
 from __future__ import annotations
 
 import numpy as np
 
+from .adaln import mx_quantize
 from .numerics import bf16_round
 
 
@@ -41,3 +63,33 @@ def wan_mlp_ref(hidden, up_w, down_w, up_b, down_b) -> np.ndarray:
 
 def ffn_flops(tokens: int, h: int, inner: int) -> float:
     return 4.0 * tokens * h * inner
+
+
+def wan_mlp_row_mx_ref(x_codes, row_scale, wu_codes, wu_scale, bu, wd_codes, wd_scale, bd) -> np.ndarray:
+    """ROW_MX MLP on ``[T, H]`` e4m3 codes (float values) with per-row fp32 ``row_scale [T]``.
+    ``wu_codes [I, H]`` / ``wd_codes [H_out, I]`` are the e4m3 weight codes (float values, K-major:
+    W^T), ``wu_scale [I]`` / ``wd_scale [H_out]`` fp32 per-channel scales, ``bu`` / ``bd`` the bf16
+    biases (float values, or None). Returns the bf16 output ``[T, H_out]`` as float32."""
+    x = np.asarray(x_codes, np.float32) * np.asarray(row_scale, np.float32).reshape(-1, 1)
+    wu = np.asarray(wu_codes, np.float32) * np.asarray(wu_scale, np.float32).reshape(-1, 1)
+    up = x @ wu.T
+    if bu is not None:
+        up = up + np.asarray(bu, np.float32).reshape(1, -1)
+    inter = gelu_tanh(up)
+    _, _, inter_dq = mx_quantize(inter)
+    wd = np.asarray(wd_codes, np.float32) * np.asarray(wd_scale, np.float32).reshape(-1, 1)
+    out = inter_dq @ wd.T
+    if bd is not None:
+        out = out + np.asarray(bd, np.float32).reshape(1, -1)
+    return bf16_round(out.astype(np.float32))
+
+
+def wan_mlp_row_mx_intermediate_ref(x_codes, row_scale, wu_codes, wu_scale, bu):
+    """The up-projection half: (codes, UE8M0 scale bytes [T, I/32], dequantised) of the MX-32
+    intermediate, for checking the up kernel's epilogue on its own."""
+    x = np.asarray(x_codes, np.float32) * np.asarray(row_scale, np.float32).reshape(-1, 1)
+    wu = np.asarray(wu_codes, np.float32) * np.asarray(wu_scale, np.float32).reshape(-1, 1)
+    up = x @ wu.T
+    if bu is not None:
+        up = up + np.asarray(bu, np.float32).reshape(1, -1)
+    return mx_quantize(gelu_tanh(up))

@@ -8,7 +8,7 @@ Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call AP
 * :func:`row_mx_qkv_proj` — FP8 QKV projection with across-heads RMS norm + rotate-half RoPE
 * :func:`wan_o_proj`, :func:`attn_out_norm2` — output projection of the d-major attention output,
   with the block's gated residual + norm2 adaLN
-* :func:`wan_mlp` — the block's FFN (GELU-tanh MLP)
+* :func:`wan_mlp` — the block's FFN (GELU-tanh MLP); :func:`row_mx_mlp` — its FP8 (ROW_MX) leaf
 * :func:`wan_block_forward` — a whole transformer block (self-attn + cross-attn + FFN, bf16 leaves)
 * :func:`cfg_gather_combine` — the CFG-parallel gather + combine of the two branch outputs
 
@@ -22,7 +22,7 @@ from .block import BlockWeights, prepare_block_weights, project_cross_kv, wan_bl
 from .build import build
 from .cfg import cfg_combine, cfg_gather_combine
 from .dit import cp_gather_sequence, cp_shard_sequence, wan_blocks_forward, wan_output_head
-from .ffn import wan_mlp
+from .ffn import quantize_mlp_weights_row_mx, row_mx_mlp, wan_mlp
 from .leaf import wan_self_attention_fp8
 from .oproj import attn_out_norm2, o_proj_gated_residual, wan_o_proj
 from .qkv import (
@@ -51,10 +51,12 @@ __all__ = [
     "pack_mx_scales",
     "prepare_block_weights",
     "project_cross_kv",
+    "quantize_mlp_weights_row_mx",
     "quantize_qkv_weight",
     "quantize_qkv_weight_mx32",
     "repack_mx_contiguous",
     "ring_attention_const_max_fwd",
+    "row_mx_mlp",
     "row_mx_qkv_proj",
     "wan_block_forward",
     "wan_blocks_forward",

@@ -88,12 +88,6 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   }
   return u;
 }
-// Two fp32 -> two e4m3 (round to nearest even, saturate to +-448); lo in byte 0.
-__device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
-  return r;
-}
 
 VOMNI_DEV void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");

@@ -398,5 +398,19 @@ VOMNI_DEV uint32_t pack_bf16x2(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// Two fp32 -> two e4m3 (round to nearest even, saturate to +-448); lo in byte 0.
+VOMNI_DEV uint16_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// GELU with the tanh approximation in fp32 (torch's gelu(approximate="tanh") formula).
+VOMNI_DEV float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float kKappa = 0.044715f;
+  const float x3 = x * x * x;
+  const float inner = kBeta * (x + kKappa * x3);
+  return 0.5f * x * (1.f + tanhf(inner));
+}
 
 }  // namespace vomni

@@ -74,15 +74,7 @@ VOMNI_DEV Tile tile_of(int t, const Params& p) {
   return Tile{band / p.m_bands, band % p.m_bands, r / rows};
 }
 
-// GELU with the tanh approximation in fp32, torch's formula (aten gelu kernel, approximate='tanh'):
-// 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3))).
-VOMNI_DEV float gelu_tanh(float x) {
-  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
-  const float kKappa = 0.044715f;
-  const float x3 = x * x * x;
-  const float inner = kBeta * (x + kKappa * x3);
-  return 0.5f * x * (1.f + tanhf(inner));
-}
+// GELU-tanh (gelu_tanh in common.cuh): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3))), fp32.
 
 // kAK: A is K-major ([M, K] rows, one 128-row box of 64 k per stage) instead of MN-major.
 template <bool kAK, int kEpi>

@@ -37,6 +37,7 @@ constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kSmemBar = kStages * kStageBytes;
 constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;
 constexpr uint32_t kIdesc = idesc_e4m3(kBM, kBN);
+constexpr uint32_t kSfAtomBytes = 512;  // one tcgen05 scale atom: 128 rows x 4 k-sub-blocks
 
 struct Params {
   int T, I, H;
@@ -48,7 +49,16 @@ struct Params {
   float* sumsq;               // [T, n_norm_heads] or null
   int n_norm_heads;           // 128-column blocks (heads) of the Q and K segments
   int* status;
+  // EPI_MX_GELU (FFN up-projection): MX-32 codes [T, I] and their scales in the tcgen05 atom layout
+  // [I/128][sf_row_blocks][512] (the A operand of the block-scaled down-projection)
+  uint8_t* codes;
+  uint8_t* sf;
+  int sf_row_blocks;
 };
+
+// Epilogues of the ROW GEMM: bf16 Y + per-head sums of squares (QKV), or bias + GELU-tanh + MX-32
+// quantisation of the result (the ROW_MX MLP's up-projection).
+enum { EPI_QKV = 0, EPI_MX_GELU = 1 };
 
 // Persistent: CTA c processes tiles c, c + gridDim.x, ... (n fastest, so the CTAs in flight share
 // the A rows and walk the whole weight, which stays L2-resident). The two 256-column TMEM
@@ -252,6 +262,7 @@ VOMNI_DEV PairTile pair_tile(int t, int m_bands, int n_tiles) {
   return PairTile{g * kGroup + r % rows, r / rows};
 }
 
+template <int kEpi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     qkv_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const Params p) {
@@ -364,6 +375,78 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool row_ok = grow < p.T;
       const uint32_t tacc = tbase + lane_addr + acc * kBN;
       const float rs = row_ok ? p.row_scale[grow] : 0.f;
+      if constexpr (kEpi == EPI_MX_GELU) {
+        // One 32-column chunk = one MX block of this thread's row: v = gelu(acc * rs * cs + bias)
+        // in fp32, UE8M0 scale = max biased exponent - 7 (clipped to [0, 255]), codes =
+        // e4m3fn(clip(v / 2^(scale - 127), +-448)). Rows past T (pad rows of the last 128-row
+        // block) get scale 127 and no codes.
+        uint8_t* crow = p.codes + static_cast<size_t>(grow) * p.I + n0;
+        const bool sf_ok = grow < p.sf_row_blocks * 128;
+        const int m = grow & 127;
+        uint8_t* sf_row = p.sf + static_cast<size_t>(grow >> 7) * kSfAtomBytes + (m & 31) * 16 + (m >> 5) * 4;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tacc + c * 32, r);
+          tmem_ld_wait(r);
+          const int col0 = n0 + c * 32;
+          const float4* cs4 = reinterpret_cast<const float4*>(p.chan_scale + col0);
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 cs = cs4[i];
+            v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) * rs * cs.x;
+            v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) * rs * cs.y;
+            v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * rs * cs.z;
+            v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * rs * cs.w;
+          }
+          if (p.bias) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 bb = b4[i];
+              const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(b2[j]);
+                v[8 * i + 2 * j] += f.x;
+                v[8 * i + 2 * j + 1] += f.y;
+              }
+            }
+          }
+          int e = 0;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v[i] = gelu_tanh(v[i]);
+            e = max(e, static_cast<int>((__float_as_uint(v[i]) >> 23) & 0xFF));
+          }
+          const int su = min(max(e - 7, 0), 255);
+          // v / 2^(su - 127) as two exact power-of-two multiplies (each factor a normal fp32)
+          const int sh = 127 - su;
+          const int sa = sh / 2, sb = sh - sa;
+          const float fa = __uint_as_float(static_cast<uint32_t>(sa + 127) << 23);
+          const float fb = __uint_as_float(static_cast<uint32_t>(sb + 127) << 23);
+          uint32_t w[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float q[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) q[j] = fminf(fmaxf((v[4 * i + j] * fa) * fb, -448.f), 448.f);
+            w[i] = e4m3x2(q[0], q[1]) | (static_cast<uint32_t>(e4m3x2(q[2], q[3])) << 16);
+          }
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + c * 32);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          }
+          if (sf_ok)
+            sf_row[static_cast<size_t>(col0 >> 7) * p.sf_row_blocks * kSfAtomBytes + ((col0 >> 5) & 3)] =
+                static_cast<uint8_t>(row_ok ? su : 127);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_acc_empty + acc * 8);
+      } else {
       float ss = 0.f, ss_lo = 0.f;
       __nv_bfloat16* yrow = p.y + static_cast<size_t>(grow) * p.I + n0;
 #pragma unroll 1
@@ -422,6 +505,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         dst[0] = ss_lo;
         dst[1] = ss;
       }
+      }
     }
   }
   tc_fence_before();
@@ -440,7 +524,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // column m1 holding the four k-sub-block scales of row 32*m1 + m0; the MMA's sf_id picks the byte.
 // Tiled order: [k-block][128-row block][512 B], so the atoms of consecutive row blocks at one
 // k-block are adjacent (a 256-column B tile's two atoms are one 1 KB copy).
-constexpr uint32_t kSfAtomBytes = 512;
 
 __global__ void mx_pack_scales_kernel(const uint8_t* __restrict__ sf, int rows, int kblk32, int row_blocks,
                                       uint8_t* __restrict__ out) {
@@ -477,7 +560,17 @@ struct MxParams {
   float* sumsq;
   int n_norm_heads;
   int* status;
+  // MX_EPI_FFN_DOWN: per-column weight scale [I], and the block's closing gated residual
+  // y <- bf16(residual + gate * bf16(acc * chan_scale + bias)) (gate fp32 [T / gate_rows, I], NULL = 1)
+  const float* chan_scale;
+  const __nv_bfloat16* residual;
+  const float* gate;
+  long long gate_rows;
 };
+
+// Epilogues of the MX-32 GEMM: bias + bf16 + per-head sums of squares (QKV), or per-column weight
+// scale + bias + bf16 (+ gated residual) (the ROW_MX MLP's down-projection).
+enum { MX_EPI_QKV = 0, MX_EPI_FFN_DOWN = 1 };
 
 VOMNI_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -671,6 +764,7 @@ constexpr uint32_t kMxPairTx = kMxPairABytes + kMxPairBBytes + kMxSfaBytes + kMx
 constexpr uint32_t kMxPairSmemBar = kMxPairStages * kMxPairStageBytes;
 constexpr uint32_t kMxPairSmemBytes = kMxPairSmemBar + 256 + 1024;
 
+template <int kEpi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     qkv_gemm_mx_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmSfa, const __grid_constant__ CUtensorMap tmSfb,
@@ -800,6 +894,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if constexpr (kEpi == MX_EPI_FFN_DOWN) {
+          // v = acc * cs + bias, eight columns at a time (keeps the live set small)
+          const float4* cs4 = reinterpret_cast<const float4*>(p.chan_scale + n0 + c * 32);
+          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + c * 32);
+#pragma unroll
+          for (int g8 = 0; g8 < 4; ++g8) {
+            const float4 ca = cs4[2 * g8], cb = cs4[2 * g8 + 1];
+            const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+            float bf[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (p.bias) {
+              const uint4 bb = b4[g8];
+              const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(b2[j]);
+                bf[2 * j] = f.x;
+                bf[2 * j + 1] = f.y;
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              pk[16 * c + 4 * g8 + j] =
+                  pack_bf16x2(__fadd_rn(__fmul_rn(v[8 * g8 + 2 * j], cs[2 * j]), bf[2 * j]),
+                              __fadd_rn(__fmul_rn(v[8 * g8 + 2 * j + 1], cs[2 * j + 1]), bf[2 * j + 1]));
+          }
+        } else {
         if (p.bias) {
           const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + c * 32);
 #pragma unroll
@@ -816,15 +936,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
-      float ss = 0.f;
+      if constexpr (kEpi == MX_EPI_FFN_DOWN) {
+        if (p.residual && grow < p.T) {
+          // (residual.float() + y.float() * gate).type_as(residual), product and sum unfused
+          const __nv_bfloat16* res = p.residual + static_cast<size_t>(grow) * p.I + n0;
+          const float* g = p.gate ? p.gate + static_cast<size_t>(grow / p.gate_rows) * p.I + n0 : nullptr;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
-        ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+          for (int i4 = 0; i4 < 16; ++i4) {
+            const uint4 rv = reinterpret_cast<const uint4*>(res)[i4];
+            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int i = 4 * i4 + j;
+              const float2 gg = g ? reinterpret_cast<const float2*>(g)[i] : make_float2(1.f, 1.f);
+              const float2 rr = __bfloat1622float2(r2[j]);
+              const float y0 = __uint_as_float(pk[i] << 16), y1 = __uint_as_float(pk[i] & 0xFFFF0000u);
+              pk[i] = pack_bf16x2(__fadd_rn(rr.x, __fmul_rn(y0, gg.x)), __fadd_rn(rr.y, __fmul_rn(y1, gg.y)));
+            }
+          }
+        }
+      }
+      float ss = 0.f;
+      if constexpr (kEpi == MX_EPI_QKV) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
+          ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+        }
       }
       if (grow < p.T) {
         uint4* dst = reinterpret_cast<uint4*>(p.y + static_cast<size_t>(grow) * p.I + n0);
@@ -987,13 +1130,16 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
   p.m_tiles = (t + qkv::kBM - 1) / qkv::kBM;
   p.n_tiles = i / qkv::kBN;
   p.status = device_status_ptr();
+  p.codes = nullptr;
+  p.sf = nullptr;
+  p.sf_row_blocks = 0;
   static int use_pair = -1;
   if (use_pair < 0) {
     const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
     use_pair = e ? atoi(e) : 1;
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kSmemBytes));
     VOMNI_CUDA_TRY(
-        cudaFuncSetAttribute(qkv::qkv_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kPairSmemBytes));
+        cudaFuncSetAttribute(qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kPairSmemBytes));
   }
   if (use_pair) {
     CUtensorMap tb2;
@@ -1001,8 +1147,8 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
     if (rc) return rc;
     const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
     const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
-    qkv::qkv_gemm_pair_kernel<<<2 * pairs, qkv::kThreads, qkv::kPairSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
-        ta, tb2, p);
+    qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV><<<2 * pairs, qkv::kThreads, qkv::kPairSmemBytes,
+                                              reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb2, p);
     VOMNI_CUDA_TRY(cudaGetLastError());
     return VOMNI_OK;
   }
@@ -1078,14 +1224,18 @@ extern "C" int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed,
   p.sumsq = sumsq;
   p.n_norm_heads = (q_dim + kv_dim) / 128;
   p.status = device_status_ptr();
+  p.chan_scale = nullptr;
+  p.residual = nullptr;
+  p.gate = nullptr;
+  p.gate_rows = 1;
   static int use_pair = -1;
   if (use_pair < 0) {
     const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
     use_pair = e ? atoi(e) : 1;
     VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         qkv::kMxSmemBytes));
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        qkv::kMxPairSmemBytes));
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kMxPairSmemBytes));
   }
   if (use_pair) {
     // X scale atoms must exist for every 128-row block a pair tile touches (pair bands are 256 rows)
@@ -1099,14 +1249,128 @@ extern "C" int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed,
     if (rc) return rc;
     const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
     const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
-    qkv::qkv_gemm_mx_pair_kernel<<<2 * pairs, qkv::kMxThreads, qkv::kMxPairSmemBytes,
-                                   reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb2, tsa, tsb, p);
+    qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV><<<2 * pairs, qkv::kMxThreads, qkv::kMxPairSmemBytes,
+                                                    reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb2, tsa, tsb, p);
     VOMNI_CUDA_TRY(cudaGetLastError());
     return VOMNI_OK;
   }
   const int n_all = p.m_tiles * p.n_tiles;
   const int grid = n_all < num_sms() ? n_all : num_sms();
   qkv::qkv_gemm_mx_kernel<<<grid, qkv::kMxThreads, qkv::kMxSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+// ---------------------------------------------------------------- ROW_MX MLP (FP8 FFN)
+// row_mx_mlp (diffusion/quantization/row_mx_kernels.py:141-198) -> nkilib mlp, ROW_MX, CTE
+// (kernels/nkilib/core/mlp/mlp_torch.py:401-600 states its arithmetic):
+//   up    = (Xq * row_scale) @ (Wu_q * wu_scale[col]) + bu       fp32
+//   inter = gelu_tanh(up), MX-32 quantised along I (_mx_quantize, mlp_torch.py:252-271)
+//   out   = (inter_q * mx_scale) @ (Wd_q * wd_scale[col]) + bd   -> bf16
+// The up GEMM is the ROW kernel with the GELU + MX epilogue (codes and scale atoms written for the
+// down GEMM directly); the down GEMM is the MX-32 block-scaled kernel with identity weight scales
+// and the per-column weight scale, bias and optional gated residual in its epilogue.
+
+extern "C" int vomni_ffn_fp8_up(const void* x_codes, const float* row_scale, const void* w_codes,
+                                const float* chan_scale, const void* bias, int t, int h, int i, void* inter_codes,
+                                void* inter_sf_packed, vomni_stream_t stream) {
+  if (!x_codes || !row_scale || !w_codes || !chan_scale || !inter_codes || !inter_sf_packed) return VOMNI_EINVAL;
+  if (t <= 0 || h <= 0 || i <= 0 || (h % qkv::kBK) || (i % qkv::kBN)) return VOMNI_EBADSHAPE;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(x_codes) | reinterpret_cast<uintptr_t>(w_codes) |
+                       reinterpret_cast<uintptr_t>(chan_scale) | reinterpret_cast<uintptr_t>(bias) |
+                       reinterpret_cast<uintptr_t>(inter_codes) | reinterpret_cast<uintptr_t>(inter_sf_packed);
+  if (al & 15) return VOMNI_EALIGN;
+  int rc = require_sm100();
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  rc = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_codes, h, t, h, qkv::kBK, qkv::kBM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
+  if (rc) return rc;
+  qkv::Params p;
+  p.T = t;
+  p.I = i;
+  p.H = h;
+  p.m_tiles = (t + qkv::kBM - 1) / qkv::kBM;
+  p.n_tiles = i / qkv::kBN;
+  p.row_scale = row_scale;
+  p.chan_scale = chan_scale;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = nullptr;
+  p.sumsq = nullptr;
+  p.n_norm_heads = 0;
+  p.status = device_status_ptr();
+  p.codes = static_cast<uint8_t*>(inter_codes);
+  p.sf = static_cast<uint8_t*>(inter_sf_packed);
+  p.sf_row_blocks = p.m_tiles;
+  static bool attr = false;
+  if (!attr) {
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_pair_kernel<qkv::EPI_MX_GELU>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kPairSmemBytes));
+    attr = true;
+  }
+  const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
+  const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
+  qkv::qkv_gemm_pair_kernel<qkv::EPI_MX_GELU><<<2 * pairs, qkv::kThreads, qkv::kPairSmemBytes,
+                                                reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+extern "C" int vomni_ffn_fp8_down(const void* inter_codes, const void* inter_sf_packed, const void* w_codes,
+                                  const void* w_sf_packed, const float* chan_scale, const void* bias, int t, int i,
+                                  int h, const void* residual, const float* gate, long long gate_rows, void* out,
+                                  vomni_stream_t stream) {
+  if (!inter_codes || !inter_sf_packed || !w_codes || !w_sf_packed || !chan_scale || !out) return VOMNI_EINVAL;
+  if (t <= 0 || h <= 0 || i <= 0 || (i % qkv::kBK) || (h % qkv::kBN)) return VOMNI_EBADSHAPE;
+  if (gate && !residual) return VOMNI_EINVAL;
+  if (gate && (gate_rows <= 0 || t % gate_rows)) return VOMNI_EBADSHAPE;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(inter_codes) | reinterpret_cast<uintptr_t>(w_codes) |
+                       reinterpret_cast<uintptr_t>(inter_sf_packed) | reinterpret_cast<uintptr_t>(w_sf_packed) |
+                       reinterpret_cast<uintptr_t>(chan_scale) | reinterpret_cast<uintptr_t>(bias) |
+                       reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(gate) |
+                       reinterpret_cast<uintptr_t>(out);
+  if (al & 15) return VOMNI_EALIGN;
+  int rc = require_sm100();
+  if (rc) return rc;
+  // K = i (intermediate), N = h (model dim): MxParams' H is the contraction, I the output width
+  CUtensorMap ta, tb, tsa, tsb;
+  rc = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, inter_codes, i, t, i, qkv::kBK, qkv::kBM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, i, h, i, qkv::kBK, 128);
+  if (rc) return rc;
+  qkv::MxParams p;
+  p.T = t;
+  p.I = h;
+  p.H = i;
+  p.m_tiles = (t + qkv::kBM - 1) / qkv::kBM;
+  p.n_tiles = h / qkv::kBN;
+  const uint64_t k128 = static_cast<uint64_t>(i / 128);
+  rc = make_tmap_2d_plain(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, inter_sf_packed, 128, k128 * p.m_tiles * 4, 128, 128, 4);
+  if (rc) return rc;
+  rc = make_tmap_2d_plain(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_sf_packed, 128, k128 * (h / 128) * 4, 128, 128, 8);
+  if (rc) return rc;
+  p.sfa = static_cast<const uint8_t*>(inter_sf_packed);
+  p.sfb = static_cast<const uint8_t*>(w_sf_packed);
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = static_cast<__nv_bfloat16*>(out);
+  p.sumsq = nullptr;
+  p.n_norm_heads = 0;
+  p.status = device_status_ptr();
+  p.chan_scale = chan_scale;
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.gate = gate;
+  p.gate_rows = gate ? gate_rows : 1;
+  static bool attr = false;
+  if (!attr) {
+    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_FFN_DOWN>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kMxPairSmemBytes));
+    attr = true;
+  }
+  const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
+  const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
+  qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_FFN_DOWN><<<2 * pairs, qkv::kMxThreads, qkv::kMxPairSmemBytes,
+                                                       reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, tsa, tsb, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }
