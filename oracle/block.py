@@ -12,8 +12,8 @@ import numpy as np
 
 from .adaln import adaln_modulate_oracle
 from .attention import torch_attend
-from .ffn import wan_mlp_ref
-from .numerics import bf16_round
+from .ffn import wan_mlp_ref, wan_mlp_row_mx_ref
+from .numerics import bf16_round, e4m3fn_from_bits
 from .oproj import wan_o_proj_ref
 from .rope import apply_rotary_emb_wan, distributed_rms_norm
 
@@ -37,8 +37,11 @@ def _attend_dmajor(q_tok, k_tok, v_tok, scale):
     return np.ascontiguousarray(bf16_round(o).transpose(0, 1, 3, 2))
 
 
-def wan_block_ref(hidden, temb, cos, sin, cross_kv, w: dict, heads: int, eps: float = 1e-6):
-    """hidden [B, S, H]; temb [B, 6, H]; cos/sin interleaved RoPE tables [S, 128]; w: reference parameter names."""
+def wan_block_ref(hidden, temb, cos, sin, cross_kv, w: dict, heads: int, eps: float = 1e-6, ffn_fp8=None):
+    """hidden [B, S, H]; temb [B, 6, H]; cos/sin interleaved RoPE tables [S, 128]; w: reference parameter names.
+    ``ffn_fp8``: (up codes [I, H], up scale [I], down codes [H, I], down scale [H]) as float arrays runs the
+    FFN as the FP8 leaf (WanFeedForwardFP8, row_mx_modules.py:549-708): norm3 with ROW quant, then the
+    ROW_MX MLP (``wan_mlp_row_mx_ref``)."""
     B, S, H = hidden.shape
     N = heads
     scale = 1.0 / np.sqrt(128)
@@ -62,6 +65,15 @@ def wan_block_ref(hidden, temb, cos, sin, cross_kv, w: dict, heads: int, eps: fl
                               w["attn2.norm_q.weight"], eps).reshape(B, S, N, 128)
     attn2 = _attend_dmajor(cq, cross_kv[0], cross_kv[1], scale)
     y2 = wan_o_proj_ref(attn2, w["attn2.o_proj_weight"], w["attn2.o_proj_bias"])
+    if ffn_fp8 is not None:
+        hidden, packed = adaln_modulate_oracle(y2, 1 + c_scl, c_shift, eps=eps, norm_type="layer_norm", quant="row",
+                                               residual=hidden)
+        packed = np.ascontiguousarray(packed).reshape(B * S, H + 4)
+        codes = e4m3fn_from_bits(packed[:, :H])
+        rs = np.ascontiguousarray(packed[:, H:]).view(np.float32).reshape(-1)
+        uc, us, dc, ds = ffn_fp8
+        f = wan_mlp_row_mx_ref(codes, rs, uc, us, w["ffn.up_bias"], dc, ds, w["ffn.down_bias"]).reshape(B, S, H)
+        return bf16_round(np.asarray(hidden, np.float32) + np.asarray(f, np.float32) * c_gate)
     hidden, norm_h = adaln_modulate_oracle(y2, 1 + c_scl, c_shift, eps=eps, norm_type="layer_norm", residual=hidden)
     f = wan_mlp_ref(norm_h, w["ffn.up_weight"], w["ffn.down_weight"], w["ffn.up_bias"], w["ffn.down_bias"])
     return bf16_round(np.asarray(hidden, np.float32) + np.asarray(f, np.float32) * c_gate)

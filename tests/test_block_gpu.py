@@ -66,6 +66,34 @@ def test_block_vs_oracle(pkg, dev, B, latent, H, I, L, cross_norm):
     assert np.abs(got - r).max() <= 0.05 * max(1.0, np.abs(r).max()), np.abs(got - r).max()
 
 
+def test_block_fp8_ffn_vs_oracle(pkg, dev):
+    """The block with the FFN's FP8 leaf (norm3 ROW-quantised, row_mx_mlp with the closing gated
+    residual) against the oracle block running the ROW_MX MLP restatement on the same codes."""
+    B, latent, H, I, L = 1, (3, 20, 20), 256, 512, 40
+    heads = H // 128
+    w, hidden, temb, ctx, cos, sin = make_block(B, latent, H, I, L, seed=3)
+    tt = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    wt = {k: (tt(v) if v is not None else None) for k, v in w.items()}
+    bw = pkg.prepare_block_weights(wt, heads, ffn_fp8=True)
+    assert bw.ffn_fp8 is not None
+    kv = pkg.project_cross_kv(tt(ctx).to(torch.bfloat16), wt["attn2.k_proj_weight"], wt["attn2.k_proj_bias"],
+                              wt["attn2.norm_k.weight"], wt["attn2.v_proj_weight"], wt["attn2.v_proj_bias"], heads)
+    rope = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.rope")
+    S = hidden.shape[1]
+    cos_rh, sin_rh = rope.rope_rotate_half_caches(tt(cos).reshape(1, S, 1, 128), tt(sin).reshape(1, S, 1, 128))
+    out = pkg.wan_block_forward(tt(hidden).to(torch.bfloat16), tt(temb), (cos_rh, sin_rh), kv, bw)
+    torch.cuda.synchronize()
+    kv_ref = ob.project_kv_ref(ctx, w["attn2.k_proj_weight"], w["attn2.k_proj_bias"], w["attn2.norm_k.weight"],
+                               w["attn2.v_proj_weight"], w["attn2.v_proj_bias"], heads, 1e-6)
+    fp8 = tuple(t.float().cpu().numpy() for t in bw.ffn_fp8)
+    ref = ob.wan_block_ref(hidden, temb, cos, sin, kv_ref, w, heads, ffn_fp8=fp8)
+    got = out.float().cpu().numpy().astype(np.float64)
+    r = ref.astype(np.float64)
+    cos_sim = (got * r).sum() / math.sqrt((got * got).sum() * (r * r).sum())
+    assert cos_sim > 0.9999, cos_sim
+    assert np.abs(got - r).max() <= 0.05 * max(1.0, np.abs(r).max()), np.abs(got - r).max()
+
+
 def test_two_blocks_and_output_head(pkg, dev):
     """A 2-block DiT slice plus the output head (wan2_2_transformer.py:1814-1829) at CP=1."""
     dit = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.dit")

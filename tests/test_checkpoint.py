@@ -94,6 +94,15 @@ def test_roundtrip_and_layouts(tmp_path):
     assert torch.equal(chan[2 * qd:], torch.full((qd,), float(src["blocks.1.self_attn.v.scale_weight"])))
     b_cat = np.concatenate([src[f"blocks.1.self_attn.{p}.bias"].float().numpy() for p in ("q", "k", "v")])[None]
     assert np.array_equal(bias.float().numpy(), bf16_round(orope.deinterleave_qk_columns(b_cat, qd, qd, 128)).reshape(-1))
+    # FP8 FFN leaf: nn.Linear [out, in] codes are the kernels' K-major W^T as stored
+    uc, us, dc, ds = ck.fp8_ffn_leaf(t, 1)
+    assert uc.dtype == torch.float8_e4m3fn and tuple(uc.shape) == (512, H) and tuple(dc.shape) == (H, 512)
+    assert torch.equal(uc.view(torch.uint8), src["blocks.1.ffn.0.weight"].view(torch.uint8))
+    assert torch.equal(dc.view(torch.uint8), src["blocks.1.ffn.2.weight"].view(torch.uint8))
+    assert torch.equal(us, torch.full((512,), float(src["blocks.1.ffn.0.scale_weight"])))
+    assert torch.equal(ds, torch.full((H,), float(src["blocks.1.ffn.2.scale_weight"])))
+    # the dequantised bf16 leaf and the FP8 leaf describe the same weights
+    assert torch.equal((uc.float() * us[:, None]).bfloat16().T, w["ffn.up_weight"])
 
 
 def test_validation_errors(tmp_path):

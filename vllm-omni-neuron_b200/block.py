@@ -28,7 +28,7 @@ import torch
 from . import _lib
 from .adaln import adaln_modulate
 from .attention import wan_cp_self_attention
-from .ffn import _gemm, wan_mlp_gated_residual
+from .ffn import _gemm, quantize_mlp_weights_row_mx, row_mx_mlp, wan_mlp_gated_residual
 from .oproj import o_proj_gated_residual
 from .rope import deinterleave_gamma_row, deinterleave_qk_columns
 
@@ -57,11 +57,18 @@ class BlockWeights:
     ffn_down_b: torch.Tensor
     heads: int
     eps: float = 1e-6
+    # FP8 FFN leaf (WanFeedForwardFP8, row_mx_modules.py:549-708): (up codes [I, H], up scale [I],
+    # down codes [H, I], down scale [H]); when set the block runs norm3 with ROW quant and row_mx_mlp
+    ffn_fp8: tuple | None = None
 
 
-def prepare_block_weights(w: dict, heads: int, eps: float = 1e-6, head_dim: int = 128) -> BlockWeights:
+def prepare_block_weights(w: dict, heads: int, eps: float = 1e-6, head_dim: int = 128,
+                          ffn_fp8: bool | tuple = False) -> BlockWeights:
     """From the reference's parameter names (``attn1.qkv_proj_weight`` [H, 3H] etc.) to
-    :class:`BlockWeights`: Q/K columns and the Q/K norm weights de-interleaved (row_mx_loaders.py:26-71)."""
+    :class:`BlockWeights`: Q/K columns and the Q/K norm weights de-interleaved (row_mx_loaders.py:26-71).
+    ``ffn_fp8``: True quantises the FFN weights per tensor for the FP8 leaf
+    (``quantize_mlp_weights_row_mx``); a ``(up codes, up scale, down codes, down scale)`` tuple (e.g.
+    ``checkpoint.fp8_ffn_leaf``) is used as given."""
     H = w["attn1.qkv_proj_weight"].shape[0]
     qd = heads * head_dim
     bf = lambda t: t.to(torch.bfloat16).contiguous()
@@ -81,6 +88,8 @@ def prepare_block_weights(w: dict, heads: int, eps: float = 1e-6, head_dim: int 
         ffn_up_w=bf(w["ffn.up_weight"]), ffn_up_b=bf(w["ffn.up_bias"]),
         ffn_down_w=bf(w["ffn.down_weight"]), ffn_down_b=bf(w["ffn.down_bias"]),
         heads=heads, eps=eps,
+        ffn_fp8=(quantize_mlp_weights_row_mx(w["ffn.up_weight"], w["ffn.down_weight"]) if ffn_fp8 is True
+                 else (tuple(ffn_fp8) if ffn_fp8 else None)),
     )
 
 
@@ -179,6 +188,13 @@ def wan_block_forward(hidden_states: torch.Tensor, temb: torch.Tensor, rotary_rh
     _norm_rope(cq, ss2, N, 0, eps, w.c_norm_q_w, None)
     attn2 = cross_attention(cq.reshape(B, S, N, 128), cross_kv[0], cross_kv[1], 1.0 / math.sqrt(128))
     hidden_states = o_proj_gated_residual(attn2, w.co_w, w.co_b, hidden_states, None)
+    if w.ffn_fp8 is not None:
+        # FP8 leaf: norm3 emits ROW-quantised rows (row_mx_modules.py:647-660), the ROW_MX MLP adds the
+        # closing gated residual in its down-projection epilogue
+        packed = adaln_modulate(hidden_states, 1 + c_scale_msa, c_shift_msa, eps=eps, norm_type="layer_norm",
+                                quant="row", row_layout="split")
+        uc, us, dc, ds = w.ffn_fp8
+        return row_mx_mlp(packed, uc, dc, us, ds, w.ffn_up_b, w.ffn_down_b, residual=hidden_states, gate=c_gate_msa)
     norm_h = adaln_modulate(hidden_states, 1 + c_scale_msa, c_shift_msa, eps=eps, norm_type="layer_norm")
     # FFN + closing gated residual
     return wan_mlp_gated_residual(hidden_states, norm_h, w.ffn_up_w, w.ffn_down_w, w.ffn_up_b, w.ffn_down_b, c_gate_msa)

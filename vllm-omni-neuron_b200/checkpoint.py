@@ -187,6 +187,19 @@ def fp8_qkv_leaf(t: dict, i: int, heads: int, head_dim: int = 128):
     return codes, chan.float(), bias, gq.to(torch.bfloat16), gk.to(torch.bfloat16)
 
 
+def fp8_ffn_leaf(t: dict, i: int):
+    """The FP8 FFN leaf's operands from block ``i`` (``ffn.0`` = up, ``ffn.2`` = down; nn.Linear
+    weights ``[out, in]`` are already the K-major W^T the kernels read): (up codes ``[I, H]``, up scale
+    ``[I]``, down codes ``[H, I]``, down scale ``[H]``), the per-tensor scalars expanded per output
+    channel (expanded_scalar_scale_loader, row_mx_loaders.py)."""
+    b = f"blocks.{i}"
+    up = t[f"{b}.ffn.0.weight"].view(torch.uint8).contiguous().view(torch.float8_e4m3fn)
+    down = t[f"{b}.ffn.2.weight"].view(torch.uint8).contiguous().view(torch.float8_e4m3fn)
+    us = torch.full((up.shape[0],), _scalar(t[f"{b}.ffn.0.scale_weight"]), dtype=torch.float32)
+    ds = torch.full((down.shape[0],), _scalar(t[f"{b}.ffn.2.scale_weight"]), dtype=torch.float32)
+    return up, us, down, ds
+
+
 def write_safetensors(path, tensors: dict, metadata: dict | None = None) -> None:
     """Minimal safetensors writer (used to build test checkpoints)."""
     rev = {v[1]: k for k, v in _DTYPES.items()}
