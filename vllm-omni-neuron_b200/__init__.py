@@ -12,7 +12,8 @@ Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call AP
 * :func:`wan_block_forward` — a whole transformer block (self-attn + cross-attn + FFN, bf16 leaves)
 * :func:`cfg_gather_combine` — the CFG-parallel gather + combine of the two branch outputs
 
-Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``) built by
+The same entry points are registered as torch custom operators ``torch.ops.b200omni.*``
+(:mod:`.ops`). Compute runs in the C-ABI library ``libvomni_b200.so`` (``include/vomni_b200.h``) built by
 :func:`build`.
 """
 
@@ -34,6 +35,7 @@ from .qkv import (
     row_mx_qkv_proj,
 )
 from .ring import destroy_rings
+from . import ops  # registers torch.ops.b200omni.*
 
 __all__ = [
     "BlockWeights",
