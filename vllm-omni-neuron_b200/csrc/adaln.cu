@@ -304,7 +304,8 @@ int launch_s(const Params& p, cudaStream_t st) {
   // Persistent grid: as many CTAs as fit on the device at once, each streaming rows through its ring.
   auto kern = p.residual ? adaln_kernel<NV, true, kS> : adaln_kernel<NV, false, kS>;
   const size_t smem = static_cast<size_t>(kS) * p.H * 2 * (p.residual ? 2 : 1);
-  VOMNI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  int rc = ensure_max_smem(kern, static_cast<int>(smem));
+  if (rc) return rc;
   int per_sm = 0;
   VOMNI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
   if (per_sm < 1) per_sm = 1;

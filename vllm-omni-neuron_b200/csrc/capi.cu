@@ -6,6 +6,8 @@
 
 #include <cstdio>
 #include <mutex>
+#include <tuple>
+#include <vector>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -81,6 +83,19 @@ static int get_encoder() {
       q != cudaDriverEntryPointSuccess || !fn)
     return VOMNI_ECUDA;
   g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return VOMNI_OK;
+}
+
+int ensure_max_smem(const void* func, int bytes) {
+  int dev = -1;
+  VOMNI_CUDA_TRY(cudaGetDevice(&dev));
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, int>> done;
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto& e : done)
+    if (std::get<0>(e) == func && std::get<1>(e) == dev && std::get<2>(e) >= bytes) return VOMNI_OK;
+  VOMNI_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.emplace_back(func, dev, bytes);
   return VOMNI_OK;
 }
 

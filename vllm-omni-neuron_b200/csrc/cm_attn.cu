@@ -800,7 +800,8 @@ int vomni::cm_attend_gated(const void* q, const void* k, const void* v, int b, i
     rc = make_tmap_3d_bf16(&tk2, k, row_elems, s_kv, b, 64, 64, static_cast<uint64_t>(kv_stride));
     if (rc) return rc;
     auto pk = poly == 8 ? cm::cm_attend_pair_kernel<8> : cm::cm_attend_pair_kernel<0>;
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kPairSmemBytes));
+    rc = ensure_max_smem(pk, cm::kPairSmemBytes);
+    if (rc) return rc;
     const int pairs = (s_q + 4 * cm::kTile - 1) / (4 * cm::kTile);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, b * h);
@@ -820,7 +821,8 @@ int vomni::cm_attend_gated(const void* q, const void* k, const void* v, int b, i
   else if (poly == 4) kern = split ? cm::cm_attend_kernel<4, true> : cm::cm_attend_kernel<4, false>;
   else if (poly == 8) kern = split ? cm::cm_attend_kernel<8, true> : cm::cm_attend_kernel<8, false>;
   else kern = split ? cm::cm_attend_kernel<0, true> : cm::cm_attend_kernel<0, false>;
-  VOMNI_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, cm::kSmemBytes));
+  rc = ensure_max_smem(kern, cm::kSmemBytes);
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((s_q + cm::kTile * cm::kQT - 1) / (cm::kTile * cm::kQT), b * h);
   cfg.blockDim = dim3(cm::kThreads);

@@ -50,6 +50,13 @@ int cm_attend_gated(const void* q, const void* k, const void* v, int b, int s_q,
                     int h, int d, long long q_stride, long long kv_stride, float softmax_scale, const float* qn2,
                     const float* kmax2, float* acc_o, float* acc_l, int flags, void* out, float* lse,
                     const unsigned* ready, unsigned ready_epoch, vomni_stream_t stream);
+// cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes) once per (kernel, device, size);
+// thread-safe. Kernels above 48 KB of dynamic shared memory need it on every device they run on.
+int ensure_max_smem(const void* func, int bytes);
+template <typename F>
+inline int ensure_max_smem(F* func, int bytes) {
+  return ensure_max_smem(reinterpret_cast<const void*>(func), bytes);
+}
 // cuStreamWriteValue32 (driver entry point fetched at run time); nullptr if unavailable.
 typedef CUresult (*StreamWriteValue32Fn)(CUstream stream, CUdeviceptr addr, cuuint32_t value, unsigned int flags);
 StreamWriteValue32Fn stream_write_value32();

@@ -279,17 +279,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 int ensure_smem_attr() {
-  static bool done = false;
-  if (!done) {
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<false, EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<false, EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_pair_kernel<true, EPI_SUMSQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    done = true;
-  }
-  return VOMNI_OK;
+  // once per kernel and device (ensure_max_smem caches)
+  int rc = 0;
+  if (!rc) rc = ensure_max_smem(gemm_bf16_pair_kernel<false, EPI_BIAS>, kSmemBytes);
+  if (!rc) rc = ensure_max_smem(gemm_bf16_pair_kernel<false, EPI_RESIDUAL>, kSmemBytes);
+  if (!rc) rc = ensure_max_smem(gemm_bf16_pair_kernel<true, EPI_BIAS>, kSmemBytes);
+  if (!rc) rc = ensure_max_smem(gemm_bf16_pair_kernel<true, EPI_GELU>, kSmemBytes);
+  if (!rc) rc = ensure_max_smem(gemm_bf16_pair_kernel<true, EPI_RESIDUAL>, kSmemBytes);
+  if (!rc) rc = ensure_max_smem(gemm_bf16_pair_kernel<true, EPI_SUMSQ>, kSmemBytes);
+  return rc;
 }
 
 }  // namespace oproj

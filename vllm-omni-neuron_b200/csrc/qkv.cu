@@ -1133,14 +1133,13 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
   p.codes = nullptr;
   p.sf = nullptr;
   p.sf_row_blocks = 0;
-  static int use_pair = -1;
-  if (use_pair < 0) {
+  static const int use_pair = [] {
     const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
-    use_pair = e ? atoi(e) : 1;
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kSmemBytes));
-    VOMNI_CUDA_TRY(
-        cudaFuncSetAttribute(qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kPairSmemBytes));
-  }
+    return e ? atoi(e) : 1;
+  }();
+  rc = use_pair ? ensure_max_smem(qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV>, qkv::kPairSmemBytes)
+                : ensure_max_smem(qkv::qkv_gemm_kernel, qkv::kSmemBytes);
+  if (rc) return rc;
   if (use_pair) {
     CUtensorMap tb2;
     rc = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
@@ -1228,15 +1227,13 @@ extern "C" int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed,
   p.residual = nullptr;
   p.gate = nullptr;
   p.gate_rows = 1;
-  static int use_pair = -1;
-  if (use_pair < 0) {
+  static const int use_pair = [] {
     const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
-    use_pair = e ? atoi(e) : 1;
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        qkv::kMxSmemBytes));
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kMxPairSmemBytes));
-  }
+    return e ? atoi(e) : 1;
+  }();
+  rc = use_pair ? ensure_max_smem(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV>, qkv::kMxPairSmemBytes)
+                : ensure_max_smem(qkv::qkv_gemm_mx_kernel, qkv::kMxSmemBytes);
+  if (rc) return rc;
   if (use_pair) {
     // X scale atoms must exist for every 128-row block a pair tile touches (pair bands are 256 rows)
     CUtensorMap tb2, tsa, tsb;
@@ -1303,12 +1300,8 @@ extern "C" int vomni_ffn_fp8_up(const void* x_codes, const float* row_scale, con
   p.codes = static_cast<uint8_t*>(inter_codes);
   p.sf = static_cast<uint8_t*>(inter_sf_packed);
   p.sf_row_blocks = p.m_tiles;
-  static bool attr = false;
-  if (!attr) {
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_pair_kernel<qkv::EPI_MX_GELU>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kPairSmemBytes));
-    attr = true;
-  }
+  rc = ensure_max_smem(qkv::qkv_gemm_pair_kernel<qkv::EPI_MX_GELU>, qkv::kPairSmemBytes);
+  if (rc) return rc;
   const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
   const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
   qkv::qkv_gemm_pair_kernel<qkv::EPI_MX_GELU><<<2 * pairs, qkv::kThreads, qkv::kPairSmemBytes,
@@ -1361,12 +1354,8 @@ extern "C" int vomni_ffn_fp8_down(const void* inter_codes, const void* inter_sf_
   p.residual = static_cast<const __nv_bfloat16*>(residual);
   p.gate = gate;
   p.gate_rows = gate ? gate_rows : 1;
-  static bool attr = false;
-  if (!attr) {
-    VOMNI_CUDA_TRY(cudaFuncSetAttribute(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_FFN_DOWN>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, qkv::kMxPairSmemBytes));
-    attr = true;
-  }
+  rc = ensure_max_smem(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_FFN_DOWN>, qkv::kMxPairSmemBytes);
+  if (rc) return rc;
   const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
   const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
   qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_FFN_DOWN><<<2 * pairs, qkv::kMxThreads, qkv::kMxPairSmemBytes,
