@@ -214,3 +214,61 @@ def test_cp_shard_gather_gloo(world):
     for rank, ok, tb in res:
         assert tb is None, tb
         assert ok, rank
+
+
+def _cfg_host_worker(rank, world, port, q):
+    try:
+        import os
+        from importlib import import_module
+
+        import torch
+        import torch.distributed as dist
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        cfg = import_module("vllm-omni-neuron_b200.cfg")
+        x = torch.full((4, 8), float(rank), dtype=torch.bfloat16)
+        outcome = None
+        try:
+            cfg.cfg_gather_combine(x, 5.0)
+        except ValueError:
+            outcome = "world"  # a CFG group must have two ranks
+        except RuntimeError:
+            outcome = "no_cpu_path"  # gathered on gloo, then the GPU combine refuses CPU tensors
+        try:
+            cfg.cfg_gather_combine((x, x), 5.0)
+            tuple_ok = False
+        except (NotImplementedError, ValueError):
+            tuple_ok = True
+        dist.destroy_process_group()
+        q.put((rank, outcome, tuple_ok, None))
+    except Exception:
+        import traceback
+
+        q.put((rank, None, False, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_cfg_gather_combine_host_checks(world):
+    """CFG gather + combine host logic on gloo ranks (cfg_parallel.py:48-71, 135-159): a group other
+    than two ranks is refused, a tuple branch output is refused, and the combine has no CPU path."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_cfg_host_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, outcome, tuple_ok, tb in res:
+        assert tb is None, tb
+        assert outcome == ("no_cpu_path" if world == 2 else "world"), (rank, outcome)
+        assert tuple_ok, rank
