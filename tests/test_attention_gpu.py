@@ -215,7 +215,8 @@ def test_errors(pkg, dev):
         pkg.ring_attention_const_max_fwd(q.float(), k, v)
 
 
-@pytest.mark.parametrize("b,s,h,training,layout", [(1, 1000, 12, False, "bhds"), (2, 777, 7, True, "bhsd")])
+@pytest.mark.parametrize("b,s,h,training,layout",
+                         [(1, 1000, 12, False, "bhds"), (2, 777, 7, True, "bhsd"), (1, 8000, 23, False, "bhds")])
 def test_host_streamed_equals_device(pkg, dev, b, s, h, training, layout):
     """Pinned host q/k/v stream through head groups; heads are independent, so the host result is
     bit-identical to the device-resident call."""
@@ -235,3 +236,24 @@ def test_host_streamed_equals_device(pkg, dev, b, s, h, training, layout):
     assert torch.equal(wan, pkg.wan_cp_self_attention(q.to(dev), k.to(dev), v.to(dev), 128 ** -0.5, 1, None, None).cpu())
     with pytest.raises(ValueError):
         attn.ring_attention_const_max_fwd(q, k, v)  # host tensors must be pinned
+
+
+def test_host_stream_groups(pkg, dev):
+    """Group sizing: one rank keeps 5-head groups; ring calls take enough heads per group to fill two
+    waves of CTA pairs; explicit small groups (ragged last group) give the device result too."""
+    attn = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.attention")
+    slots = torch.cuda.get_device_properties(dev).multi_processor_count // 2
+    for s, h in ((32760, 40), (16380, 40), (8190, 40), (4095, 40), (8000, 23)):
+        assert attn._host_group_heads(s, h, dev, 1) == 5
+        gh = attn._host_group_heads(s, h, dev, 8)
+        assert 5 <= gh <= h
+        assert gh * -(-s // 512) >= min(h * -(-s // 512), 2 * slots) or gh == 5
+    assert attn._host_group_heads(4095, 40, dev, 8) == 20 and attn._host_group_heads(8190, 40, dev, 4) == 10
+    g = torch.Generator().manual_seed(12)
+    q, k, v = ((torch.randn(1, 1000, 7, 128, generator=g) * 0.5).to(torch.bfloat16) for _ in range(3))
+    fn = lambda a, b_, c: attn.attention_local(a, b_, c, out_layout="bhds")
+    host = attn._host_streamed(fn, q.pin_memory(), k.pin_memory(), v.pin_memory(), out_layout="bhds", training=False,
+                               group_heads=3)
+    devr = attn.attention_local(q.to(dev), k.to(dev), v.to(dev), out_layout="bhds")
+    torch.cuda.synchronize()
+    assert torch.equal(host, devr.cpu())

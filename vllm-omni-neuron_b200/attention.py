@@ -67,6 +67,20 @@ def token_major(t: torch.Tensor) -> tuple[torch.Tensor, int]:
 
 
 _HOST_GROUP_HEADS = 5
+
+
+def _host_group_heads(s: int, h: int, dev: torch.device, world: int = 1) -> int:
+    """Heads per host-streamed group. One rank (PCIe-bound, cheap calls): 5, the finest split that
+    measured fastest. A CP ring (every call pays an all-reduce, block copies and several pass
+    launches): the finest split whose passes still fill two waves of CTA pairs (a pair covers 512
+    query rows of one head on two SMs), e.g. 20 heads for S_loc = 4095, 10 for 8190."""
+    if world <= 1:
+        return min(h, _HOST_GROUP_HEADS)
+    pairs_per_head = -(-s // 512)
+    slots = max(1, torch.cuda.get_device_properties(dev).multi_processor_count // 2)
+    g_min = max(_HOST_GROUP_HEADS, -(-2 * slots // pairs_per_head))
+    groups = max(1, h // g_min)
+    return -(-h // groups)
 _AUX_STREAMS: dict = {}
 
 
@@ -85,7 +99,8 @@ def _copy_2d(dst_ptr, dpitch, src_ptr, spitch, width, height, stream):
 
 def _host_streamed(fn, q, k, v, *, out_layout: str, training: bool, alternate: bool = True,
                    group_heads: int | None = None):
-    """Run ``fn(q_dev, k_dev, v_dev) -> out | (out, lse)`` over head groups of pinned host q/k/v.
+    """Run ``fn(q_dev, k_dev, v_dev) -> out | (out, lse)`` over head groups of pinned host q/k/v
+    (``group_heads`` heads per group, default 5).
 
     Group g's host->device copies run on a copy stream, its attention alternates between the
     caller's stream and a second compute stream (so one group's tail wave overlaps the next group;
@@ -217,7 +232,10 @@ def ring_attention_const_max_fwd(
             return ring_attention_const_max_fwd(qd, kd, vd, replica_groups, num_workers, softmax_scale, training,
                                                 torch.float32, kv_prefetch_depth, group=group, out_layout=out_layout)
 
-        res = _host_streamed(dev_call, q, k, v, out_layout=out_layout, training=training, alternate=num_workers <= 1)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gh = _host_group_heads(q.shape[1], q.shape[2], dev, num_workers)
+        res = _host_streamed(dev_call, q, k, v, out_layout=out_layout, training=training, alternate=num_workers <= 1,
+                             group_heads=gh)
         return (res[0], res[1].to(lse_dtype)) if training else res
     _check_qkv(q, k, v)
     if num_workers <= 1:
