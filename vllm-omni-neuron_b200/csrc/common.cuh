@@ -170,30 +170,6 @@ VOMNI_DEV void cluster_sync() {
 VOMNI_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
-// try_wait with acquire at cluster scope, for barriers that threads of the peer CTA arrive on.
-VOMNI_DEV bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, "
-      "p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-VOMNI_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int* status, int code,
-                                 uint64_t budget_ns = kWaitBudgetNs) {
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity, 200000u)) return true;
-    if (*abort) return false;
-    if (globaltimer() - t0 > budget_ns) {
-      *abort = 1;
-      if (status) atomicCAS(status, 0, code);
-      return false;
-    }
-  }
-}
 // Tile load into this CTA's shared memory whose completion is counted on the mbarrier at
 // shared::cluster address `bar_cluster` (this CTA's or its pair leader's). Not a multicast.
 VOMNI_DEV void tma_load_3d_pair(const CUtensorMap* m, uint32_t bar_cluster, void* dst, int x, int y, int z) {
