@@ -1,9 +1,8 @@
 """Generate the golden vectors that pin the CPU oracle to the reference's own code.
 
-Run in the build container, where the reference checkout is mounted (default
-``/root/reference``; override with ``VOMNI_REFERENCE``)::
+Run where the reference checkout is available, with its root in ``VOMNI_REFERENCE``::
 
-    python tests/golden/make_golden.py
+    VOMNI_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Only the reference's dependency-light torch/numpy pieces are executed (the NKI kernels
 cannot run without a Trainium toolchain):
@@ -39,7 +38,10 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get("VOMNI_REFERENCE", "/root/reference")) / "vllm_omni_neuron"
+_REF_ROOT = os.environ.get("VOMNI_REFERENCE")
+if not _REF_ROOT:
+    raise SystemExit("set VOMNI_REFERENCE to the root of the reference checkout")
+REF = Path(_REF_ROOT) / "vllm_omni_neuron"
 OUT = Path(__file__).resolve().parent
 
 
