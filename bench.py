@@ -393,6 +393,12 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         heads_s, rows_s = 1, 512
         qs, ks, vs = cpu_sample_arrays(q, k, v, heads_s, rows_s)
+        try:  # all host threads, also when a launcher pinned OMP_NUM_THREADS=1
+            from threadpoolctl import threadpool_limits
+
+            _pool = threadpool_limits(limits=os.cpu_count() or 1)  # noqa: F841
+        except Exception:
+            pass
         val, el, fl = cpu_attention_sample(qs, ks, vs, min_seconds=10.0)
         cpu = {"value": round(val, 5), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
                "sample": f"_torch_attend restated (oracle/attention.py torch_attend, numpy fp32): {heads_s} head x {rows_s} query rows x {S} keys, repeated {el:.1f}s ({fl/1e9:.0f} GFLOP)"}
@@ -848,6 +854,14 @@ def run_reference(args, world, rank, cfg, flops_layer, emit):
         return
     import numpy as np
 
+    # torchrun starts every rank with OMP_NUM_THREADS=1; the reference arm runs alone on rank 0 and
+    # uses all host threads, as a CPU deployment of the reference would.
+    try:
+        from threadpoolctl import threadpool_limits
+
+        _pool = threadpool_limits(limits=os.cpu_count() or 1)  # noqa: F841 (kept for the whole run)
+    except Exception:
+        pass
     S = cfg["S"]
     rng = np.random.default_rng(0)
     heads_s, rows_s = 1, 1024
