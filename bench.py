@@ -624,8 +624,8 @@ def run_oproj(args, emit):
             "oproj_gemm": {"ms": round(t_p, 4), "flops": flops, "TFLOP/s": round(flops / t_p / 1e9, 1),
                            "frac_of_measured_bf16_burst": round(flops / t_p / 1e9 / bf16, 4)},
             "oproj_gemm_gated_residual": {"ms": round(t_f, 4), "TFLOP/s": round(flops / t_f / 1e9, 1)},
-            "fused_step": {"ms": round(t_fn, 4), "kernels": "oproj_pair_kernel (residual epilogue) + adaln_kernel"},
-            "unfused_step": {"ms": round(t_un, 4), "kernels": "oproj_pair_kernel + adaln_kernel (residual step)"},
+            "fused_step": {"ms": round(t_fn, 4), "kernels": "gemm_bf16_pair_kernel<0,1> (residual epilogue) + adaln_kernel"},
+            "unfused_step": {"ms": round(t_un, 4), "kernels": "gemm_bf16_pair_kernel<0,0> + adaln_kernel (residual step)"},
         },
         "clocks": clocks,
         "gpu_launches": 5 * n,
