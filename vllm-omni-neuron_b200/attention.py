@@ -98,9 +98,9 @@ def _copy_2d(dst_ptr, dpitch, src_ptr, spitch, width, height, stream):
 
 
 def _host_streamed(fn, q, k, v, *, out_layout: str, training: bool, alternate: bool = True,
-                   group_heads: int | None = None):
+                   group_heads: int | None = None, world: int = 1):
     """Run ``fn(q_dev, k_dev, v_dev) -> out | (out, lse)`` over head groups of pinned host q/k/v
-    (``group_heads`` heads per group, default 5).
+    (``group_heads`` heads per group, default ``_host_group_heads`` for a ring of ``world`` ranks).
 
     Group g's host->device copies run on a copy stream, its attention alternates between the
     caller's stream and a second compute stream (so one group's tail wave overlaps the next group;
@@ -122,7 +122,7 @@ def _host_streamed(fn, q, k, v, *, out_layout: str, training: bool, alternate: b
     host_o = torch.empty(o_shape, dtype=torch.bfloat16, pin_memory=True)
     n_lse = 128 * (-(-s // 128))
     host_lse = torch.empty((b, h, 128, n_lse // 128), dtype=torch.float32, pin_memory=True) if training else None
-    gh = max(1, int(group_heads or _HOST_GROUP_HEADS))
+    gh = max(1, int(group_heads or _host_group_heads(s, h, dev, world)))
     row = h * d * esz
     h2d.wait_stream(main)
     alt.wait_stream(main)
@@ -232,10 +232,8 @@ def ring_attention_const_max_fwd(
             return ring_attention_const_max_fwd(qd, kd, vd, replica_groups, num_workers, softmax_scale, training,
                                                 torch.float32, kv_prefetch_depth, group=group, out_layout=out_layout)
 
-        dev = torch.device("cuda", torch.cuda.current_device())
-        gh = _host_group_heads(q.shape[1], q.shape[2], dev, num_workers)
         res = _host_streamed(dev_call, q, k, v, out_layout=out_layout, training=training, alternate=num_workers <= 1,
-                             group_heads=gh)
+                             world=num_workers)
         return (res[0], res[1].to(lse_dtype)) if training else res
     _check_qkv(q, k, v)
     if num_workers <= 1:
