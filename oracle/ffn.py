@@ -22,11 +22,14 @@ CTE mode, following its PyTorch reference ``_mlp_ref_standard``
     out   = (inter_q * s) @ (Wd_q * wd_scale) + bd           (:593-596), returned as bf16 (the
                                                              kernel's ``output_dtype="bfloat16"``)
 
-Partly pinned: the MX block size is ``_q_height * _q_width`` from
-``nkilib.core.mlp.mlp_tkg.projection_mx_constants``, which is not in the reference tree; 32 (the MX
-block of the rest of the reference, ``adaln_quant_torch.py:151-175``) is assumed, and the
-exponent clip to [0, 255] (a UE8M0 byte) only differs from the unclipped reference for blocks whose
-largest magnitude is below 2^-120.
+Pinned by ``tests/golden/mlp_row_mx.npz``: outputs of the reference's own ``_mlp_ref_standard`` and
+``_mx_quantize`` run from its source (``make_golden.py mlp_row_mx``), equal bit for bit. That run
+stands in for helpers outside the reference tree: the MX block size ``_q_height * _q_width`` (from the
+unvendored ``nkilib.core.mlp.mlp_tkg.projection_mx_constants``) is taken as 32, the MX block of the
+rest of the reference (``adaln_quant_torch.py:151-175``); the fp8 round trip, the fp32 exponent
+extraction and the weight-layout undo are replaced by their plain equivalents. The exponent clip to
+[0, 255] (a UE8M0 byte) only differs from the unclipped reference in the scale of all-zero or
+sub-2^-120 blocks, whose codes and dequantised values are the same.
 """
 
 from __future__ import annotations

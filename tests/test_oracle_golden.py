@@ -191,3 +191,25 @@ def test_cfg_combine_matches_torch_eager(dtype, scale):
         ref = (neg + scale * (pos - neg)).float().numpy()
         got = ocfg.cfg_gather_combine_ref([pos.float().numpy(), neg.float().numpy()], scale, dtype == "bf16")
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_mlp_row_mx_oracle_vs_reference_golden(golden):
+    """The ROW_MX MLP restatement equals the reference's own ``_mlp_ref_standard`` (ROW_MX, CTE,
+    GELU-tanh; mlp_torch.py:401-600) bit for bit, and the MX-32 quantiser equals its ``_mx_quantize``
+    (:252-271) on codes and dequantised values (fixtures: ``make_golden.py mlp_row_mx``)."""
+    from oracle import adaln as oad
+    from oracle import ffn as off
+
+    g = golden("mlp_row_mx.npz")
+    for tag in ("a", "b"):
+        codes = e4m3fn_from_bits(g[f"{tag}|codes"])
+        uc = e4m3fn_from_bits(g[f"{tag}|uc"])  # [H, I] (x @ W layout)
+        dc = e4m3fn_from_bits(g[f"{tag}|dc"])  # [I, H]
+        H, I = uc.shape
+        y = off.wan_mlp_row_mx_ref(codes, g[f"{tag}|rs"], uc.T, np.full(I, g[f"{tag}|su"], np.float32), g[f"{tag}|bu"],
+                                   dc.T, np.full(H, g[f"{tag}|sd"], np.float32), g[f"{tag}|bd"])
+        assert np.array_equal(y.view(np.uint32), g[f"{tag}|y"].astype(np.float32).view(np.uint32)), tag
+    codes, _, deq = oad.mx_quantize(g["mxq|x"])
+    assert np.array_equal(codes, g["mxq|codes"])
+    ref_deq = (g["mxq|codes"].astype(np.float64) * g["mxq|scale"]).astype(np.float32)
+    assert np.array_equal(deq, ref_deq)
