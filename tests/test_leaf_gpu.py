@@ -58,3 +58,45 @@ def test_fp8_leaf_vs_oracle(pkg, dev):
     r = ref.astype(np.float64)
     cos_sim = (got * r).sum() / math.sqrt((got * got).sum() * (r * r).sum())
     assert cos_sim >= 0.9999 and np.abs(got - r).max() <= 2e-2, (cos_sim, np.abs(got - r).max())
+
+
+def test_fp8_cross_attention_leaf_vs_oracle(pkg, dev):
+    """WanCrossAttentionFP8 up to the attention output (row_mx_modules.py:478-542): separate ROW FP8
+    Q/K/V projections, across-heads RMS norm on Q and K (no RoPE), exact attention over the text
+    tokens, against the oracle chain on the same FP8 codes."""
+    B, S, L, H, heads = 1, 300, 64, 256, 2
+    qd = heads * 128
+    g = torch.Generator().manual_seed(8)
+    hidden = torch.randn(B, S, H, generator=g).to(torch.bfloat16).to(dev)
+    ctx = torch.randn(B, L, H, generator=g).to(torch.bfloat16).to(dev)
+    ws = {n: (torch.randn(H, qd, generator=g) * 0.03).to(dev) for n in "qkv"}
+    bs = {n: (torch.randn(qd, generator=g) * 0.05).to(torch.bfloat16).to(dev) for n in "qkv"}
+    gq = (1 + 0.1 * torch.randn(qd, generator=g)).to(torch.bfloat16).to(dev)
+    gk = (1 + 0.1 * torch.randn(qd, generator=g)).to(torch.bfloat16).to(dev)
+    quant = {n: pkg.quantize_qkv_weight(ws[n], qd, 0) for n in "qkv"}
+    packed = pkg.adaln_modulate(hidden, None, None, eps=1e-6, norm_type="layer_norm", quant="row")
+    packed_ctx = pkg.adaln_modulate(ctx, None, None, eps=1e-6, norm_type="none", quant="row")
+    kv = pkg.project_cross_kv_fp8(packed_ctx, quant["k"][0], quant["k"][1], bs["k"], gk, quant["v"][0], quant["v"][1],
+                                  bs["v"], num_heads=heads)
+    out = pkg.wan_cross_attention_fp8(packed, quant["q"][0], quant["q"][1], bs["q"], gq, kv, num_heads=heads)
+    torch.cuda.synchronize()
+    assert tuple(out.shape) == (B, heads, 128, S)
+
+    def proj(pk, n, gamma):
+        codes, chan = quant[n]
+        kw = dict(num_heads=heads, head_dim=128, num_kv_heads=0, eps=1e-6)
+        if gamma is not None:
+            kw["gamma_q"] = gamma.float().cpu().numpy()
+        return oq.row_mx_qkv_ref(pk.view(torch.uint8).cpu().numpy()[0], e4m3fn_from_bits(codes.view(torch.uint8).cpu().numpy()).T,
+                                 chan.cpu().numpy(), bs[n].float().cpu().numpy(), **(kw if gamma is not None else {}))
+
+    q = proj(packed, "q", gq).reshape(B, S, heads, 128)
+    k = proj(packed_ctx, "k", gk).reshape(B, L, heads, 128)
+    v = proj(packed_ctx, "v", None).reshape(B, L, heads, 128)
+    np.testing.assert_allclose(kv[1].float().cpu().numpy(), v, atol=1e-2, rtol=1e-2)
+    ref = oat.torch_attend(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3), 1 / math.sqrt(128))
+    ref = ref.transpose(0, 1, 3, 2)  # d-major
+    got = out.float().cpu().numpy().astype(np.float64)
+    r = ref.astype(np.float64)
+    cos_sim = (got * r).sum() / math.sqrt((got * got).sum() * (r * r).sum())
+    assert cos_sim >= 0.9999 and np.abs(got - r).max() <= 2e-2, (cos_sim, np.abs(got - r).max())

@@ -24,7 +24,7 @@ from .build import build
 from .cfg import cfg_combine, cfg_gather_combine
 from .dit import cp_gather_sequence, cp_shard_sequence, wan_blocks_forward, wan_output_head
 from .ffn import quantize_mlp_weights_row_mx, row_mx_mlp, wan_mlp
-from .leaf import wan_self_attention_fp8
+from .leaf import project_cross_kv_fp8, wan_cross_attention_fp8, wan_self_attention_fp8
 from .oproj import attn_out_norm2, o_proj_gated_residual, wan_o_proj
 from .qkv import (
     mx32_qkv_proj,
@@ -52,6 +52,7 @@ __all__ = [
     "o_proj_gated_residual",
     "pack_mx_scales",
     "prepare_block_weights",
+    "project_cross_kv_fp8",
     "project_cross_kv",
     "quantize_mlp_weights_row_mx",
     "quantize_qkv_weight",
@@ -63,6 +64,7 @@ __all__ = [
     "wan_block_forward",
     "wan_blocks_forward",
     "wan_cp_self_attention",
+    "wan_cross_attention_fp8",
     "wan_mlp",
     "wan_o_proj",
     "wan_output_head",

@@ -1,4 +1,6 @@
-"""The FP8 self-attention leaf: fused ROW FP8 QKV projection -> const-max (ring) attention.
+"""The FP8 attention leaves: ROW FP8 projections -> const-max attention.
+
+Self-attention (``wan_self_attention_fp8``): fused ROW FP8 QKV projection -> const-max (ring) attention.
 
 Mirrors ``WanSelfAttentionFP8.forward`` (vllm_omni_neuron/diffusion/quantization/row_mx_modules.py:
 340-404) up to the attention output (the o-projection that follows, :404, is outside this path):
@@ -9,6 +11,14 @@ Mirrors ``WanSelfAttentionFP8.forward`` (vllm_omni_neuron/diffusion/quantization
 3. ``tensor_split`` into Q/K/V token-major views (:390-393) — passed to the attention with their row
    stride, no copy;
 4. ``wan_cp_self_attention`` (:395-403), d-major ``[B, N, D, S_loc]`` result.
+
+Cross-attention (``wan_cross_attention_fp8``, ``project_cross_kv_fp8``): ``WanCrossAttentionFP8``
+(row_mx_modules.py:407-548) up to the attention output: separate ROW FP8 Q, K and V projections of
+the packed rows (Q from the block's norm2 adaLN, K/V from the once-quantised text context), the
+across-heads RMS norm on Q and on K (each passing its gamma as the kernel's Q gamma, no RoPE; V not
+normed; :478-542), then exact attention over the text tokens. The FP8 o-projection that follows
+(``row_mx_o_proj``, :544-546) quantises its activation inside an NKI kernel whose source is not in
+the reference tree and is not part of this leaf.
 """
 
 from __future__ import annotations
@@ -18,6 +28,7 @@ import math
 import torch
 
 from .attention import wan_cp_self_attention
+from .block import cross_attention
 from .qkv import row_mx_qkv_proj
 from .rope import rope_rotate_half_caches
 
@@ -66,3 +77,50 @@ def wan_self_attention_fp8(
     return wan_cp_self_attention(
         query, key, value, scale if scale else 1.0 / math.sqrt(head_dim), cp_size, cp_group, cp_replica_groups
     )
+
+
+def project_cross_kv_fp8(
+    packed_encoder_hidden_states,
+    k_proj_weight: torch.Tensor,
+    k_proj_w_scale: torch.Tensor,
+    k_proj_bias: torch.Tensor | None,
+    norm_k_weight: torch.Tensor | None,
+    v_proj_weight: torch.Tensor,
+    v_proj_w_scale: torch.Tensor,
+    v_proj_bias: torch.Tensor | None,
+    *,
+    num_heads: int,
+    head_dim: int = 128,
+    eps: float = 1e-6,
+):
+    """``WanCrossAttentionFP8.project_kv`` (row_mx_modules.py:509-542): K with the across-heads RMS
+    norm, V plain, from the packed ``[B, L, H + 4]`` text rows; token-major ``[B, L, N, D]`` K and V.
+    Weights: ``[N*D, H]`` FP8 codes with per-channel scales (``quantize_qkv_weight(w, N*D, 0)``)."""
+    key = row_mx_qkv_proj(packed_encoder_hidden_states, k_proj_weight, k_proj_w_scale, k_proj_bias,
+                          num_heads=num_heads, head_dim=head_dim, num_kv_heads=0, qk_norm_pre_rope=True,
+                          qk_norm_pre_rope_q_gamma=norm_k_weight, norm_eps=eps)
+    value = row_mx_qkv_proj(packed_encoder_hidden_states, v_proj_weight, v_proj_w_scale, v_proj_bias,
+                            num_heads=num_heads, head_dim=head_dim, num_kv_heads=0)
+    return key.unflatten(-1, (num_heads, head_dim)), value.unflatten(-1, (num_heads, head_dim))
+
+
+def wan_cross_attention_fp8(
+    hidden_states,
+    q_proj_weight: torch.Tensor,
+    q_proj_w_scale: torch.Tensor,
+    q_proj_bias: torch.Tensor | None,
+    norm_q_weight: torch.Tensor | None,
+    cross_kv,
+    *,
+    num_heads: int,
+    head_dim: int = 128,
+    eps: float = 1e-6,
+    scale: float | None = None,
+):
+    """``WanCrossAttentionFP8._project_query`` (row_mx_modules.py:478-507) and the attention over the
+    text K/V (``project_cross_kv_fp8``): packed ``[B, S, H + 4]`` rows in, d-major ``[B, N, D, S]`` out."""
+    query = row_mx_qkv_proj(hidden_states, q_proj_weight, q_proj_w_scale, q_proj_bias, num_heads=num_heads,
+                            head_dim=head_dim, num_kv_heads=0, qk_norm_pre_rope=True,
+                            qk_norm_pre_rope_q_gamma=norm_q_weight, norm_eps=eps)
+    query = query.unflatten(-1, (num_heads, head_dim))
+    return cross_attention(query, cross_kv[0], cross_kv[1], scale if scale else 1.0 / math.sqrt(head_dim))

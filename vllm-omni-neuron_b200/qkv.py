@@ -40,6 +40,8 @@ def quantize_qkv_weight(w: torch.Tensor, q_size: int, kv_size: int):
     chan = torch.empty(w.shape[1], dtype=torch.float32, device=w.device)
     codes = torch.empty_like(w)
     for lo, hi in ((0, q_size), (q_size, q_size + kv_size), (q_size + kv_size, q_size + 2 * kv_size)):
+        if hi == lo:  # a single projection (kv_size = 0), e.g. the cross-attention's separate Q, K, V
+            continue
         sc = torch.clamp(w[:, lo:hi].abs().amax() / 448.0, min=1e-12)
         codes[:, lo:hi] = w[:, lo:hi] / sc
         chan[lo:hi] = sc
