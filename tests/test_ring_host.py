@@ -55,7 +55,7 @@ def _shard(rank, b=1, s=96, h=2, seed=11):
     return [bf16_round(rng.standard_normal((b, s, h, 128)).astype(np.float32) * 0.7) for _ in range(3)]
 
 
-def _emulated_ring_worker(rank, world, port, out_q):
+def _emulated_ring_worker(rank, world, port, out_q, fault=None):
     try:
         import torch
         import torch.distributed as dist
@@ -81,11 +81,18 @@ def _emulated_ring_worker(rank, world, port, out_q):
         dist.all_gather(ks, torch.from_numpy(k))
         dist.all_gather(vs, torch.from_numpy(v))
         # gather buffer in ring-step order: slot j holds step j+1's block
-        gk = np.concatenate([ks[ring.source_rank(rank, world, s)].numpy() for s in range(1, world)], axis=1)
-        gv = np.concatenate([vs[ring.source_rank(rank, world, s)].numpy() for s in range(1, world)], axis=1)
+        src = (lambda s: (rank + s) % world) if fault == "order" else (lambda s: ring.source_rank(rank, world, s))
+        gk = np.concatenate([ks[src(s)].numpy() for s in range(1, world)], axis=1)
+        gv = np.concatenate([vs[src(s)].numpy() for s in range(1, world)], axis=1)
         acc, ssum = oat.const_max_partial(q, k, v, c, scale)  # pass 0: local block
         s_loc = q.shape[1]
-        for first, count in ring.phase_plan(world)[1:]:
+        plan = ring.phase_plan(world)[1:]
+        if fault == "drop":  # the last pass loses its last block
+            first, count = plan[-1]
+            plan = plan[:-1] + ([(first, count - 1)] if count > 1 else [])
+        if fault == "dup":  # the first remote block is accumulated twice
+            plan = plan + [plan[0]]
+        for first, count in plan:
             sl = slice(first * s_loc, (first + count) * s_loc)
             a, sm = oat.const_max_partial(q, gk[:, sl], gv[:, sl], c, scale)
             acc += a
@@ -119,6 +126,28 @@ def test_ring_schedule_gloo(ring, world):
         # pass order differs from the step order only by fp32 summation order
         assert e_ring <= 1e-2, (rank, e_ring)
         assert e_exact <= 2e-2, (rank, e_exact)
+
+
+@pytest.mark.parametrize("world,fault", [(2, "drop"), (3, "drop"), (3, "dup"), (3, "order")])
+def test_ring_schedule_faults_gloo(ring, world, fault):
+    """Faults planted in the emulated schedule: a dropped or duplicated K/V block is caught by the
+    comparison with the oracle; a wrong rotation direction (each remote block still used once) gives
+    the right result, because const-max partials combine by plain addition in any order."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_emulated_ring_worker, args=(r, world, port, q, fault)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, e_ring, e_exact, tb in res:
+        assert tb is None, tb
+        if fault == "order":
+            assert e_ring <= 1e-2 and e_exact <= 2e-2, (rank, e_ring, e_exact)
+        else:
+            assert e_ring > 5e-2 and e_exact > 5e-2, (rank, fault, e_ring, e_exact)
 
 
 def _dying_rank_worker(rank, world, port, out_q):
