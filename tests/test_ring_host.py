@@ -31,6 +31,19 @@ def test_phase_plan_covers_each_block_once(ring, world):
     assert slots == list(range(world - 1))
 
 
+def test_phase_plan_knob(ring, monkeypatch):
+    """VOMNI_RING_PLAN replaces the doubling pass sizes; the last size repeats; bad values are refused."""
+    monkeypatch.setenv("VOMNI_RING_PLAN", "2,5")
+    assert ring.phase_plan(8) == [(-1, 1), (0, 2), (2, 5)]
+    monkeypatch.setenv("VOMNI_RING_PLAN", "3")
+    assert ring.phase_plan(8) == [(-1, 1), (0, 3), (3, 3), (6, 1)]
+    monkeypatch.setenv("VOMNI_RING_PLAN", "0")
+    with pytest.raises(Exception):
+        ring.phase_plan(8)
+    monkeypatch.delenv("VOMNI_RING_PLAN")
+    assert ring.phase_plan(8) == [(-1, 1), (0, 1), (1, 2), (3, 4)]
+
+
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_ring_order(ring, world):
     for r in range(world):
