@@ -447,64 +447,64 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(lead_acc_empty + acc * 8);
       } else {
-      float ss = 0.f, ss_lo = 0.f;
-      __nv_bfloat16* yrow = p.y + static_cast<size_t>(grow) * p.I + n0;
+        float ss = 0.f, ss_lo = 0.f;
+        __nv_bfloat16* yrow = p.y + static_cast<size_t>(grow) * p.I + n0;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tacc + c * 32, r);
-        tmem_ld_wait(r);
-        const int col0 = n0 + c * 32;
-        const float4* cs4 = reinterpret_cast<const float4*>(p.chan_scale + col0);
-        float v[32];
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tacc + c * 32, r);
+          tmem_ld_wait(r);
+          const int col0 = n0 + c * 32;
+          const float4* cs4 = reinterpret_cast<const float4*>(p.chan_scale + col0);
+          float v[32];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 cs = cs4[i];
-          v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) * rs * cs.x;
-          v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) * rs * cs.y;
-          v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * rs * cs.z;
-          v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * rs * cs.w;
-        }
-        if (p.bias) {
-          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
+          for (int i = 0; i < 8; ++i) {
+            const float4 cs = cs4[i];
+            v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) * rs * cs.x;
+            v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) * rs * cs.y;
+            v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * rs * cs.z;
+            v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * rs * cs.w;
+          }
+          if (p.bias) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 bb = b4[i];
-            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+            for (int i = 0; i < 4; ++i) {
+              const uint4 bb = b4[i];
+              const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(b2[j]);
-              v[8 * i + 2 * j] += f.x;
-              v[8 * i + 2 * j + 1] += f.y;
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(b2[j]);
+                v[8 * i + 2 * j] += f.x;
+                v[8 * i + 2 * j + 1] += f.y;
+              }
             }
           }
-        }
-        uint32_t pk[16];
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-          const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
-          ss = fmaf(lo, lo, fmaf(hi, hi, ss));
-        }
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(yrow + c * 32);
+          for (int i = 0; i < 16; ++i) {
+            pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+            const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
+            ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+          }
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(yrow + c * 32);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
+          if (c == 3) {
+            ss_lo = ss;
+            ss = 0.f;
+          }
         }
-        if (c == 3) {
-          ss_lo = ss;
-          ss = 0.f;
+        // This warp's rows of the accumulator have been read: tell the leader's MMA warp.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_acc_empty + acc * 8);
+        if (row_ok && p.sumsq && 2 * nt < p.n_norm_heads) {
+          float* dst = p.sumsq + static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt;
+          dst[0] = ss_lo;
+          dst[1] = ss;
         }
-      }
-      // This warp's rows of the accumulator have been read: tell the leader's MMA warp.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(lead_acc_empty + acc * 8);
-      if (row_ok && p.sumsq && 2 * nt < p.n_norm_heads) {
-        float* dst = p.sumsq + static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt;
-        dst[0] = ss_lo;
-        dst[1] = ss;
-      }
       }
     }
   }
@@ -920,22 +920,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
                               __fadd_rn(__fmul_rn(v[8 * g8 + 2 * j + 1], cs[2 * j + 1]), bf[2 * j + 1]));
           }
         } else {
-        if (p.bias) {
-          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + c * 32);
+          if (p.bias) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + c * 32);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 bb = b4[i];
-            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
+            for (int i = 0; i < 4; ++i) {
+              const uint4 bb = b4[i];
+              const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(b2[j]);
-              v[8 * i + 2 * j] += f.x;
-              v[8 * i + 2 * j + 1] += f.y;
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(b2[j]);
+                v[8 * i + 2 * j] += f.x;
+                v[8 * i + 2 * j + 1] += f.y;
+              }
             }
           }
-        }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
         }
       }
       tc_fence_before();
