@@ -385,13 +385,23 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
       return VOMNI_ECUDA;
   }
   VOMNI_CUDA_TRY(cudaEventRecord(R->ev_copies_done, R->copy_stream));
-  // 5. passes: local block, then ranges of arrived blocks; fp32 partial, normalise on the last
+  // 5. passes: local block, then ranges of arrived blocks; fp32 partial, normalise on the last.
+  // Every return from here joins the copy stream first (also on an error), so no later work on the
+  // caller stream can overlap this call's copies.
+  auto join_copies = [&](int status) {
+    const cudaError_t e = cudaStreamWaitEvent(st, R->ev_copies_done, 0);
+    if (status == VOMNI_OK && e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return static_cast<int>(VOMNI_ECUDA);
+    }
+    return status;
+  };
   int first[64], count[64];
   const int np = vomni_ring_phase_plan(N, first, count, 64);
-  if (np < 2) return VOMNI_EINVAL;
+  if (np < 2) return join_copies(VOMNI_EINVAL);
   rc = vomni_cm_attend_strided(q, k, v, b, s_loc, s_loc, 0, s_loc, h, d, q_stride, kv_stride, softmax_scale, R->qn2,
                                R->kmax2, R->acc_o, R->acc_l, 0, nullptr, nullptr, stream);
-  if (rc) return rc;
+  if (rc) return join_copies(rc);
   const int s_kv = (N - 1) * s_loc;
   for (int p = 1; p < np; ++p) {
     const int last_step = first[p] + count[p];  // ring step of the last block in this pass
@@ -401,17 +411,20 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
       // and only its epilogue (the accumulator read-modify-write) waits for that pass.
       fl |= VOMNI_CM_OVERLAP;
     } else {
-      VOMNI_CUDA_TRY(cudaStreamWaitEvent(st, R->ev_block[last_step], 0));
+      const cudaError_t e = cudaStreamWaitEvent(st, R->ev_block[last_step], 0);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return join_copies(VOMNI_ECUDA);
+      }
     }
     rc = cm_attend_gated(q, R->gather_k, R->gather_v, b, s_loc, s_kv, first[p] * s_loc, count[p] * s_loc, h, d,
                          q_stride, 0, softmax_scale, R->qn2, R->kmax2, R->acc_o, R->acc_l, fl, out, lse,
                          write_value ? R->ready + last_step : nullptr, epoch, stream);
-    if (rc) return rc;
+    if (rc) return join_copies(rc);
   }
   // Join the copy stream: this rank's copies of its peers' send buffers are complete before any later
   // work on the caller stream (the next call's all_reduce included).
-  VOMNI_CUDA_TRY(cudaStreamWaitEvent(st, R->ev_copies_done, 0));
-  return VOMNI_OK;
+  return join_copies(VOMNI_OK);
 }
 
 extern "C" int vomni_ring_attention(vomni_ring* R, const void* q, const void* k, const void* v, void* out, float* lse,
