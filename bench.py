@@ -197,7 +197,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=list(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tokens", type=int, default=0, help="c3 / oproj: override the token count (small case for profiling)")
+    ap.add_argument("--tokens", type=int, default=0, help="c3 / oproj / ffn / ffn_fp8: override the token count (small case for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
