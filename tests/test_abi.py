@@ -49,3 +49,24 @@ def test_host_validation_without_gpu(lib):
     # workspace too small
     assert L.vomni_cm_attention_local(p, p, p, p, None, 1, 128, 1, 128, 0.1, 0, p, 16, None) == 8
     assert L.vomni_cm_workspace_bytes(1, 128, 2, 128) >= 2 * 128 * 4
+
+
+def test_host_validation_new_entry_points(lib):
+    """The FFN FP8 GEMMs, the CFG combine and the ready-wait self-test check their arguments before
+    any CUDA call."""
+    L = lib.load()
+    p = ctypes.c_void_p(16)
+    q = ctypes.c_void_p(18)
+    assert L.vomni_cfg_combine(None, p, p, 8, 0, 1.0, None) == 1  # null pointer
+    assert L.vomni_cfg_combine(p, p, p, 8, 7, 1.0, None) == 1  # unknown dtype
+    assert L.vomni_cfg_combine(p, p, p, 0, 1, 1.0, None) == 0  # nothing to do
+    assert L.vomni_cfg_combine(q, p, p, 8, 1, 1.0, None) == 3  # misaligned
+    # up: h % 128 != 0; i % 256 != 0
+    assert L.vomni_ffn_fp8_up(p, p, p, p, None, 8, 100, 512, p, p, None) == 2
+    assert L.vomni_ffn_fp8_up(p, p, p, p, None, 8, 256, 200, p, p, None) == 2
+    # down: gate without residual; t not a multiple of gate_rows
+    assert L.vomni_ffn_fp8_down(p, p, p, p, p, None, 8, 512, 256, None, p, 8, p, None) == 1
+    assert L.vomni_ffn_fp8_down(p, p, p, p, p, None, 8, 512, 256, p, p, 3, p, None) == 2
+    res = ctypes.c_int(-1)
+    assert L.vomni_selftest_ready_wait(0, 0, ctypes.byref(res), None) == 1
+    assert L.vomni_selftest_ready_wait(100, 3, ctypes.byref(res), None) == 1
