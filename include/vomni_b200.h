@@ -64,6 +64,11 @@ VOMNI_API int vomni_selftest_bounded_wait(unsigned budget_us, int* result_host, 
  * post = 0: nothing posts it, the wait gives up, *result_host = 0 and the status word reads
  * VOMNI_DEV_TIMEOUT_BASE + 0x7E. Synchronises `stream`. */
 VOMNI_API int vomni_selftest_ready_wait(unsigned budget_us, int post, int* result_host, vomni_stream_t stream);
+/* Evaluates, for n device floats x, the FMA-pipe exponential 2^x that the attention kernel uses for
+ * a share of its softmax probabilities (Cody-Waite range reduction + degree-3 minimax polynomial in
+ * packed fp32 pairs; inputs below -126 clamp to about 2^-126) into device y. A test hook so that the
+ * method can be checked against exact 2^x; no counterpart in the reference. Stream-ordered. */
+VOMNI_API int vomni_selftest_exp2_poly(const float* x, float* y, long long n, vomni_stream_t stream);
 /* Stream-ordered 2-D copy (height rows of width bytes; pitches in bytes) between any two of host
  * (pinned) and device memory: the host-resident attention entry streams head groups with it.
  * No counterpart in the reference (its inputs are always device-resident). */
@@ -296,8 +301,9 @@ VOMNI_API int vomni_ring_source_rank(int rank, int world, int step);
  * the library until the process exits), so the call allocates nothing; the caller still passes
  * q, k, v, out (and lse). Limit: vomni_cm_workspace_bytes(b, s, h, d) <= 8 MiB (about
  * b*h*s <= 2.09 million query rows); larger shapes return VOMNI_EWORKSPACE.
- * The first call on a device looks up the array's device address with that device current; make
- * that first call before any stream capture. All calls share the one array and it keeps the last
+ * The first call on a device (and the first after a cudaDeviceReset of it) looks up the array's
+ * device address with that device current and caches it; make that first call before any stream
+ * capture. All calls share the one array and it keeps the last
  * call's contents (the key-max slots are cleared by each call before use): calls that overlap on
  * the GPU (different streams, or threads without ordering) race on it. */
 VOMNI_API int vomni_cm_attention_local_noalloc(const void* q, const void* k, const void* v, void* out, float* lse, int b,

@@ -257,3 +257,57 @@ def test_host_stream_groups(pkg, dev):
     devr = attn.attention_local(q.to(dev), k.to(dev), v.to(dev), out_layout="bhds")
     torch.cuda.synchronize()
     assert torch.equal(host, devr.cpu())
+
+
+def test_c1_full_shape_vs_oracle(pkg, dev):
+    """BASELINE config 1 at its stated shape: B=1, S=4096, H=40, Q/K/V ~ N(0,1)*0.5 (seeds 0,1,2),
+    softmax scale 1/sqrt(128), against the exact fp32 attention and the const-max restatement."""
+    b, s, h = 1, 4096, 40
+    qkv = []
+    for seed in (0, 1, 2):
+        g = torch.Generator().manual_seed(seed)
+        qkv.append((torch.randn(b, s, h, 128, generator=g) * 0.5).to(torch.bfloat16))
+    o = pkg.ring_attention_const_max_fwd(*(x.to(dev) for x in qkv))
+    torch.cuda.synchronize()
+    qn, kn, vn = (x.float().numpy() for x in qkv)
+    got = _f32(o)
+    ref_exact = oat.torch_attend(*(np.transpose(x, (0, 2, 1, 3)) for x in (qn, kn, vn)), 1 / math.sqrt(128))
+    _cmp(got, ref_exact, "C1 vs exact")
+    ref_cm = oat.const_max_ring_attention([qn], [kn], [vn])[0]
+    _cmp(got, ref_cm, "C1 vs const-max oracle")
+    from importlib import import_module
+
+    assert import_module("vllm-omni-neuron_b200._lib").device_status() == 0
+
+
+def test_exp2_poly_error_bound(pkg, dev):
+    """The FMA-pipe exponential the softmax uses for a share of its probabilities: relative error
+    against exact 2^x (float64) within the polynomial's fitted bound plus fp32 evaluation rounding
+    (1e-4) wherever the result is a normal number, and 0 below x = -125.5 as the flush-to-zero
+    MUFU exponential gives 0 under 2^-126. Also within that bound of CUDA's own exp2 on the GPU."""
+    from importlib import import_module
+
+    lib = import_module("vllm-omni-neuron_b200._lib")
+    L = lib.load()
+    xs = torch.cat([torch.linspace(-125.49, 1.0, 1 << 20, dtype=torch.float64).float(),
+                    torch.tensor([0.0, -0.5, 0.5, -1.0, -64.25, -125.0, -125.49, -125.5, -125.6, -126.0, -127.0,
+                                  -200.0, -1e30, float("-inf")])])
+    x = xs.to(dev)
+    y = torch.empty_like(x)
+    lib.check(L.vomni_selftest_exp2_poly(x.data_ptr(), y.data_ptr(), x.numel(), torch.cuda.current_stream().cuda_stream),
+              "vomni_selftest_exp2_poly")
+    cuda_exp2 = torch.exp2(x)
+    torch.cuda.synchronize()
+    xd = xs.double().numpy()
+    got = y.cpu().double().numpy()
+    exact = np.exp2(xd)
+    normal = xd > -125.5
+    rel = np.abs(got[normal] - exact[normal]) / exact[normal]
+    assert rel.max() <= 1e-4, rel.max()
+    assert (got[~normal] == 0).all()
+    cu = cuda_exp2.cpu().double().numpy()
+    assert (np.abs(got[normal] - cu[normal]) / cu[normal]).max() <= 1e-4
+    # odd element count: the last value is evaluated on its own
+    lib.check(L.vomni_selftest_exp2_poly(x.data_ptr(), y.data_ptr(), 3, torch.cuda.current_stream().cuda_stream), "odd n")
+    torch.cuda.synchronize()
+    assert np.allclose(y[:3].cpu().double().numpy(), exact[:3], rtol=1e-4, atol=0)

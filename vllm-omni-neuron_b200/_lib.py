@@ -24,6 +24,7 @@ SIGNATURES = {
     "vomni_device_status": (c_int, [ctypes.POINTER(c_int), c_int]),
     "vomni_selftest_bounded_wait": (c_int, [ctypes.c_uint, ctypes.POINTER(c_int), P]),
     "vomni_selftest_ready_wait": (c_int, [ctypes.c_uint, c_int, ctypes.POINTER(c_int), P]),
+    "vomni_selftest_exp2_poly": (c_int, [P, P, ctypes.c_longlong, P]),
     "vomni_memcpy_2d_async": (c_int, [P, c_size_t, P, c_size_t, c_size_t, c_size_t, P]),
     "vomni_cm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "vomni_cm_prologue": (c_int, [P, P, c_int, c_int, c_int, c_int, P, P, P]),

@@ -8,10 +8,12 @@
 // and partial results of different key ranges (ring steps) combine by plain addition; one final
 // normalise o_i = O_i / max(l_i, 1e-37).
 //
-// Kernel layout (one CTA = two 128-row query tiles of one (batch, head)):
-//   warp 0      TMA producer: both Q tiles once, then K/V 128-key tiles into 2-stage rings (no multicast)
-//   warp 1      TMEM owner + MMA issuer (one elected lane): S_t = Q_t K^T (SS form), O_t += P_t V (TS
-//               form, P read straight from TMEM)
+// Kernel layout: a cluster of two CTAs on two SMs (tcgen05 cta_group::2) covers 2 x 256 query rows
+// of one (batch, head); query tile t of the pair is 256 rows, 128 in each CTA. Per CTA:
+//   warp 0      TMA producer: its halves of both Q tiles once, then K/V 128-key tiles into 2-stage
+//               rings (no multicast)
+//   warp 1      TMEM owner; in the even CTA also the MMA issuer (one elected lane):
+//               S_t = Q_t K^T (SS form), O_t += P_t V (TS form, P read straight from TMEM)
 //   warps 2..5  softmax of query tile 0, warps 6..9 of query tile 1: one query row per thread (TMEM
 //               lane), P = exp2(S*scale*log2e - c*log2e) written back to TMEM as bf16 over S, then
 //               the epilogue (normalise / partial write). The two warpgroups ping-pong: while one
@@ -28,32 +30,31 @@
 #include <cstdlib>
 #include <mutex>
 
+// Exponentials per 16 consecutive key columns of a row that run on the FMA pipe (the packed
+// polynomial of common.cuh) instead of MUFU ex2, counted in column pairs out of 8. A build-time
+// constant (nvcc -DVOMNI_CM_POLY_PAIRS=k); the library has exactly one attention kernel.
+#ifndef VOMNI_CM_POLY_PAIRS
+#define VOMNI_CM_POLY_PAIRS 0
+#endif
+
 namespace vomni {
 namespace cm {
 
-constexpr int kTile = 128;  // query rows per tile and keys per tile
+constexpr int kTile = 128;  // query rows per tile (per CTA) and keys per tile
 constexpr int kD = 128;     // head dim (the reference asserts 128, ring_attention_const_max_fwd.py:1026)
 constexpr int kQT = 2;      // query tiles per CTA (two softmax warpgroups ping-pong on the tensor pipe)
 constexpr int kThreads = 64 + 128 * kQT;
 constexpr uint32_t kTileBytes = kTile * kD * 2;  // 32 KB: one bf16 [128 x 128] tile
 constexpr uint32_t kHalfBytes = kTileBytes / 2;  // 16 KB: one [128 x 64] swizzled half
+constexpr int kPolyPairs = VOMNI_CM_POLY_PAIRS;
+static_assert(kPolyPairs >= 0 && kPolyPairs <= 8, "VOMNI_CM_POLY_PAIRS is a count out of 8 column pairs");
 
-// smem map (offsets from a 1024-aligned base)
-constexpr uint32_t kSmemQ = 0;                          // kQT tiles
-constexpr uint32_t kSmemK = kSmemQ + kQT * kTileBytes;  // 2 stages
-constexpr uint32_t kSmemV = kSmemK + 2 * kTileBytes;    // 2 stages
-constexpr uint32_t kSmemBar = kSmemV + 2 * kTileBytes;  // barriers + scalars
-constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + alignment slack
-
-// S_FULL: one barrier per query tile t at index 2t. P_FULL: one per (tile t, key half h) at 2t + h;
-// the whole-tile pipeline uses only h = 0.
+// S_FULL: one barrier per query tile t at index 2t. P_FULL: one per (tile t, key half h) at 2t + h.
 enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 13, O_FULL = 17, NBAR = 18 };
 
 // TMEM columns: tile t owns S_t = [t*128, t*128+128) (P_t, bf16, aliases its first 64 columns) and
 // O_t = [256 + t*128, 256 + t*128 + 128).
 constexpr uint32_t kColS = 0, kColO = 256;
-constexpr uint32_t kIdescQK = idesc_bf16(128, 128, false);
-constexpr uint32_t kIdescPV = idesc_bf16(128, 128, true);
 
 struct Params {
   int s_q;          // query rows per (batch, head)
@@ -74,71 +75,53 @@ struct Params {
   unsigned ready_epoch;
 };
 
-// S = Q_t K^T: 8 MMAs of K=16 over the two 64-wide swizzled halves (K-major SW128: +32 B per step).
-// Descriptors are built once per CTA; the start-address field (bits 0-13, address >> 4) is then
-// advanced by plain integer adds (no carry: shared addresses stay below 256 KB).
-__device__ __forceinline__ void issue_qk(uint32_t d_s, uint64_t q_desc, uint64_t k_desc) {
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint64_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
-    mma_f16_ss(d_s, q_desc + off, k_desc + off, kIdescQK, kk > 0);
-  }
-}
-// O_t += P_t V over keys [64*hf, 64*hf + 64).
-__device__ __forceinline__ void issue_pv_half(uint32_t d_o, uint32_t p_tmem, uint64_t v_desc, int hf, bool accumulate) {
-#pragma unroll
-  for (int k2 = 0; k2 < 4; ++k2) {
-    const int kk = hf * 4 + k2;
-    mma_f16_ts(d_o, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV, (accumulate || kk > 0) ? 1u : 0u);
-  }
-}
-// O_t += P_t V: P from TMEM (8 columns of packed bf16 per 16 keys), V as an MN-major SW128 operand
-// (16 keys = two 8-row groups = +2048 B; the two 64-wide d halves are 16 KB apart).
-__device__ __forceinline__ void issue_pv(uint32_t d_o, uint32_t p_tmem, uint64_t v_desc, bool accumulate) {
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk)
-    mma_f16_ts(d_o, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV, (accumulate || kk > 0) ? 1u : 0u);
+// Column pair i (of 16 in a 32-column chunk) takes the FMA-pipe exponential when it is one of the
+// kPolyPairs pairs spread evenly over each group of 8.
+__host__ __device__ constexpr bool poly_pair(int i) {
+  return ((i % 8 + 1) * kPolyPairs) / 8 > ((i % 8) * kPolyPairs) / 8;
 }
 
-// One 32-column chunk of one query row: p = 2^(s*scale*log2e - c*log2e), summed into four
-// independent accumulators (no serial add chain) and packed to bf16 pairs for the PV MMA.
-// kPoly: every kPoly-th column goes through the FMA-pipe polynomial instead of the MUFU ex2 unit
-// (0 = none). kMask: columns at or past `valid` (keys outside this pass) contribute 0.
-template <int kPoly, bool kMask>
-VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], float scale_log2, float neg_c2, int valid, float (&acc)[4],
+// One 32-column chunk of one query row: p = 2^(s*scale*log2e - c*log2e), packed to bf16 pairs for
+// the PV MMA, and the row sum accumulated from those same bf16 values: the reference sums exactly
+// the bf16 P it multiplies, through the ones column of [V|1] (attention_const_max.py:307-311,
+// 370-379). The scale-and-shift and the sum run as packed fp32 pairs; two independent accumulator
+// pairs keep the add chain short. kMask: columns at or past `valid` (keys outside this pass)
+// contribute 0.
+template <bool kMask>
+VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], uint64_t scale2, uint64_t neg_c2, int valid, uint64_t (&acc)[2],
                              uint32_t (&pk)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const float x0 = fmaf(__uint_as_float(s[2 * i]), scale_log2, neg_c2);
-    const float x1 = fmaf(__uint_as_float(s[2 * i + 1]), scale_log2, neg_c2);
-    float p0 = (kPoly > 0 && ((2 * i) % (kPoly > 0 ? kPoly : 1)) == kPoly - 1) ? exp2_poly(x0) : ex2_approx(x0);
-    float p1 = (kPoly > 0 && ((2 * i + 1) % (kPoly > 0 ? kPoly : 1)) == kPoly - 1) ? exp2_poly(x1) : ex2_approx(x1);
+    const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), scale2, neg_c2);
+    float x0, x1, p0, p1;
+    f2_unpack(x, x0, x1);
+    if (poly_pair(i)) {
+      exp2_poly2(x0, x1, p0, p1);
+    } else {
+      p0 = ex2_approx(x0);
+      p1 = ex2_approx(x1);
+    }
     if (kMask) {
       p0 = (2 * i < valid) ? p0 : 0.f;
       p1 = (2 * i + 1 < valid) ? p1 : 0.f;
     }
-    acc[i & 3] += p0 + p1;
     pk[i] = pack_bf16x2(p0, p1);
+    acc[i & 1] = f2_add(acc[i & 1], f2_pack(__uint_as_float(pk[i] << 16), __uint_as_float(pk[i] & 0xffff0000u)));
   }
+}
+
+// Signal that this warp's P columns are in TMEM: one arrival per warp on the pair leader's barrier.
+VOMNI_DEV void publish_p(uint32_t bar_cluster) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(bar_cluster);
 }
 
 // Whole-tile softmax that publishes P in two halves: keys 0-63 (P columns 0-31) are signalled on
 // `p_lo` as soon as they are in TMEM, so the PV MMAs over them overlap the exponentials of keys
 // 64-127. The S columns 64-127 are loaded while keys 0-63 are computed.
-// Signal that this thread's (or, for a CTA pair, this warp's) P columns are in TMEM.
-template <bool kPair>
-VOMNI_DEV void publish_p(uint64_t* bar, uint32_t bar_cluster) {
-  if (kPair) {
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(bar_cluster);
-  } else {
-    mbar_arrive(bar);
-  }
-}
-
-template <int kPoly, bool kMask, bool kPair>
-VOMNI_DEV void softmax_tile_split(uint32_t col_s, float scale_log2, float neg_c2, int valid, float (&acc)[4],
-                                  uint64_t* p_lo, uint32_t p_lo_cluster) {
+template <bool kMask>
+VOMNI_DEV void softmax_tile_split(uint32_t col_s, uint64_t scale2, uint64_t neg_c2, int valid, uint64_t (&acc)[2],
+                                  uint32_t p_lo_cluster) {
   uint32_t s0[32], s1[32], s2[32], s3[32];
   tmem_ld32(col_s, s0);
   tmem_ld32(col_s + 32, s1);
@@ -147,43 +130,18 @@ VOMNI_DEV void softmax_tile_split(uint32_t col_s, float scale_log2, float neg_c2
   tmem_ld32(col_s + 64, s2);
   tmem_ld32(col_s + 96, s3);
   uint32_t pk[16];
-  softmax_chunk<kPoly, kMask>(s0, scale_log2, neg_c2, valid, acc, pk);
+  softmax_chunk<kMask>(s0, scale2, neg_c2, valid, acc, pk);
   tmem_st16(col_s, pk);
-  softmax_chunk<kPoly, kMask>(s1, scale_log2, neg_c2, valid - 32, acc, pk);
+  softmax_chunk<kMask>(s1, scale2, neg_c2, valid - 32, acc, pk);
   tmem_st16(col_s + 16, pk);
   tmem_st_wait();
   tc_fence_before();
-  publish_p<kPair>(p_lo, p_lo_cluster);
+  publish_p(p_lo_cluster);
   tmem_ld_wait(s2);
   tmem_ld_wait(s3);
-  softmax_chunk<kPoly, kMask>(s2, scale_log2, neg_c2, valid - 64, acc, pk);
+  softmax_chunk<kMask>(s2, scale2, neg_c2, valid - 64, acc, pk);
   tmem_st16(col_s + 32, pk);
-  softmax_chunk<kPoly, kMask>(s3, scale_log2, neg_c2, valid - 96, acc, pk);
-  tmem_st16(col_s + 48, pk);
-}
-
-template <int kPoly, bool kMask>
-VOMNI_DEV void softmax_tile(uint32_t col_s, float scale_log2, float neg_c2, int valid, float (&acc)[4]) {
-  // The whole 128-column S row is loaded with four back-to-back TMEM loads and one wait, so the
-  // TMEM latency is paid once per tile; P chunk ch then lands on columns [16ch, 16ch+16) of the
-  // same S region (all of it already read).
-  uint32_t s0[32], s1[32], s2[32], s3[32];
-  tmem_ld32(col_s, s0);
-  tmem_ld32(col_s + 32, s1);
-  tmem_ld32(col_s + 64, s2);
-  tmem_ld32(col_s + 96, s3);
-  tmem_ld_wait(s0);
-  tmem_ld_wait(s1);
-  tmem_ld_wait(s2);
-  tmem_ld_wait(s3);
-  uint32_t pk[16];
-  softmax_chunk<kPoly, kMask>(s0, scale_log2, neg_c2, valid, acc, pk);
-  tmem_st16(col_s, pk);
-  softmax_chunk<kPoly, kMask>(s1, scale_log2, neg_c2, valid - 32, acc, pk);
-  tmem_st16(col_s + 16, pk);
-  softmax_chunk<kPoly, kMask>(s2, scale_log2, neg_c2, valid - 64, acc, pk);
-  tmem_st16(col_s + 32, pk);
-  softmax_chunk<kPoly, kMask>(s3, scale_log2, neg_c2, valid - 96, acc, pk);
+  softmax_chunk<kMask>(s3, scale2, neg_c2, valid - 96, acc, pk);
   tmem_st16(col_s + 48, pk);
 }
 
@@ -195,10 +153,9 @@ VOMNI_DEV void release_stages(uint64_t* bars, int j) {
 }
 
 // Softmax + epilogue warpgroups (warps 2..9): query tile t = (warp-2)/4, one query row per thread.
-// q_base: first query row of this CTA's tile 0; tile_stride: rows between its tiles. kPair: the P
+// q_base: first query row of this CTA's tile 0; tile_stride: rows between its tiles. The P
 // barriers live in the pair leader and take one arrival per warp (p_full_cluster = their
-// shared::cluster address); otherwise they are local and take one arrival per thread.
-template <int kPoly, bool kSplit, bool kPair>
+// shared::cluster address).
 VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort_flag, uint32_t tbase, int warp, int lane,
                             int q_base, int tile_stride, int bh, int n_tiles, uint32_t p_full_cluster) {
   const int t = (warp - 2) >> 2;  // query tile of this warpgroup
@@ -217,41 +174,31 @@ VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort
     const float c32 = p.scale * sqrtf(p.kmax2[bh] * p.qn2[rowidx]);
     c = __bfloat162float(__float2bfloat16_rn(c32));
   }
-  const float neg_c2 = -c * 1.4426950408889634f;
+  const float neg_c = -c * 1.4426950408889634f;
+  const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+  const uint64_t neg_c2 = f2_pack(neg_c, neg_c);
   // One thread of the last tile's warpgroup frees the K/V stages: S_{last}(j) complete means
   // every QK of step j (and, issued before it, every PV of step j-1) has finished reading them.
   const bool releaser = (t == kQT - 1) && row == 0;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  uint64_t acc[2] = {0ull, 0ull};  // two (fp32, fp32) pairs, +0.0f bit patterns
   bool ok = true;
   for (int j = 0; j < n_tiles && ok; ++j) {
     const int valid = p.n_keys - j * kTile;  // keys of this tile inside the pass's range
-    if (kSplit) {
-      if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
-      tc_fence_after();
-      if (releaser) release_stages(bars, j);
-      if (valid >= kTile)
-        softmax_tile_split<kPoly, false, kPair>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t],
-                                                p_full_cluster + (2 * t) * 8);
-      else
-        softmax_tile_split<kPoly, true, kPair>(col_s, p.scale_log2, neg_c2, valid, acc, &bars[P_FULL + 2 * t],
-                                               p_full_cluster + (2 * t) * 8);
-      tmem_st_wait();
-      tc_fence_before();
-      publish_p<kPair>(&bars[P_FULL + 2 * t + 1], p_full_cluster + (2 * t + 1) * 8);
-    } else {
-      if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
-      tc_fence_after();
-      if (releaser) release_stages(bars, j);
-      if (valid >= kTile)
-        softmax_tile<kPoly, false>(col_s, p.scale_log2, neg_c2, valid, acc);
-      else
-        softmax_tile<kPoly, true>(col_s, p.scale_log2, neg_c2, valid, acc);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bars[P_FULL + 2 * t]);
-    }
+    if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+    tc_fence_after();
+    if (releaser) release_stages(bars, j);
+    if (valid >= kTile)
+      softmax_tile_split<false>(col_s, scale2, neg_c2, valid, acc, p_full_cluster + (2 * t) * 8);
+    else
+      softmax_tile_split<true>(col_s, scale2, neg_c2, valid, acc, p_full_cluster + (2 * t) * 8);
+    tmem_st_wait();
+    tc_fence_before();
+    publish_p(p_full_cluster + (2 * t + 1) * 8);
   }
-  const float rowsum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  float a0, a1, a2, a3;
+  f2_unpack(acc[0], a0, a1);
+  f2_unpack(acc[1], a2, a3);
+  const float rowsum = (a0 + a1) + (a2 + a3);
   // ---------------------------------------------------------- epilogue
   if (ok && mbar_wait(&bars[O_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) {
     tc_fence_after();
@@ -313,151 +260,13 @@ VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort
   }
 }
 
-template <int kPoly, bool kSplit>
-__global__ void __launch_bounds__(kThreads, 1)
-    cm_attend_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + NBAR * 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + NBAR * 8 + 4);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  pdl_trigger();
-  const int q0 = blockIdx.x * kTile * kQT;
-  const int bh = blockIdx.y;
-  const int b = bh / p.heads;
-  const int h = bh % p.heads;
-  const int n_tiles = (p.n_keys + kTile - 1) / kTile;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bars[Q_FULL], 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[K_FULL + i], 1);
-      mbar_init(&bars[K_EMPTY + i], 1);
-      mbar_init(&bars[V_FULL + i], 1);
-      mbar_init(&bars[V_EMPTY + i], 1);
-    }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&bars[S_FULL + i], 1);
-      mbar_init(&bars[P_FULL + i], 128);
-    }
-    mbar_init(&bars[O_FULL], 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_base_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tmem_base_slot;
-
-  uint8_t* sQ = smem + kSmemQ;
-  uint8_t* sK = smem + kSmemK;
-  uint8_t* sV = smem + kSmemV;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      const int x0 = h * kD;
-      mbar_expect_tx(&bars[Q_FULL], kQT * kTileBytes);
-      for (int t = 0; t < kQT; ++t) {
-        tma_load_3d(&tmQ, &bars[Q_FULL], sQ + t * kTileBytes, x0, q0 + t * kTile, b);
-        tma_load_3d(&tmQ, &bars[Q_FULL], sQ + t * kTileBytes + kHalfBytes, x0 + 64, q0 + t * kTile, b);
-      }
-      const bool kv_ready = !p.ready || ready_wait(p.ready, p.ready_epoch, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 10);
-      for (int j = 0; kv_ready && j < n_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int k_row = p.k_start + j * kTile;
-        if (j >= 2 && !mbar_wait(&bars[K_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 1)) break;
-        mbar_expect_tx(&bars[K_FULL + st], kTileBytes);
-        tma_load_3d(&tmK, &bars[K_FULL + st], sK + st * kTileBytes, x0, k_row, b);
-        tma_load_3d(&tmK, &bars[K_FULL + st], sK + st * kTileBytes + kHalfBytes, x0 + 64, k_row, b);
-        if (j >= 2 && !mbar_wait(&bars[V_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 2)) break;
-        mbar_expect_tx(&bars[V_FULL + st], kTileBytes);
-        tma_load_3d(&tmV, &bars[V_FULL + st], sV + st * kTileBytes, x0, k_row, b);
-        tma_load_3d(&tmV, &bars[V_FULL + st], sV + st * kTileBytes + kHalfBytes, x0 + 64, k_row, b);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // Order per key tile j (tile t = 0, 1 alternating): PV_t(j-1) then QK_t(j). QK_t(j) overwrites
-    // S_t/P_t, which PV_t(j-1) reads; tcgen05.mma ops of one thread execute in issue order.
-    if (lane == 0) {
-      const uint64_t q_desc = make_sdesc(smem_u32(sQ), 16, 1024, kLayoutSW128);
-      const uint64_t k_desc = make_sdesc(smem_u32(sK), 16, 1024, kLayoutSW128);
-      const uint64_t v_desc = make_sdesc(smem_u32(sV), kHalfBytes, 1024, kLayoutSW128);
-      constexpr uint64_t kTileDesc = kTileBytes >> 4;
-      bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 3) &&
-                mbar_wait(&bars[K_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < kQT; ++t) {
-          issue_qk(tbase + kColS + t * 128, q_desc + t * kTileDesc, k_desc);
-          tc_commit(&bars[S_FULL + 2 * t]);
-        }
-      }
-      for (int j = 1; ok && j <= n_tiles; ++j) {
-        const int jj = j - 1;
-        const int vs = jj & 1, ks = j & 1;
-        for (int t = 0; t < kQT && ok; ++t) {
-          const uint32_t d_o = tbase + kColO + t * 128, d_s = tbase + kColS + t * 128;
-          if (kSplit) {
-            // PV over keys 0-63 as soon as that half of P is in TMEM, then keys 64-127; the next QK
-            // follows (it overwrites S/P, which these PV MMAs read: issue order suffices).
-            for (int hf = 0; hf < 2 && ok; ++hf) {
-              if (!mbar_wait(&bars[P_FULL + 2 * t + hf], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) { ok = false; break; }
-              if (t == 0 && hf == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) { ok = false; break; }
-              tc_fence_after();
-              issue_pv_half(d_o, d_s, v_desc + vs * kTileDesc, hf, jj > 0);
-            }
-            if (!ok) break;
-          } else {
-            if (!mbar_wait(&bars[P_FULL + 2 * t], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 5)) { ok = false; break; }
-            if (t == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 6)) { ok = false; break; }
-            tc_fence_after();
-            issue_pv(d_o, d_s, v_desc + vs * kTileDesc, jj > 0);
-          }
-          if (j < n_tiles) {
-            if (t == 0 && !mbar_wait(&bars[K_FULL + ks], (j >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 4)) { ok = false; break; }
-            tc_fence_after();
-            issue_qk(d_s, q_desc + t * kTileDesc, k_desc + ks * kTileDesc);
-            tc_commit(&bars[S_FULL + 2 * t]);
-          }
-        }
-      }
-      tc_commit(&bars[O_FULL]);
-    }
-  } else {
-    // ------------------------------------------------------------ softmax + epilogue
-    softmax_role<kPoly, kSplit, false>(p, bars, abort_flag, tbase, warp, lane, q0, kTile, bh, n_tiles, 0u);
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tbase, 512);
-  }
-  pdl_wait();  // this grid completes only after the pass it overlapped (also on an abort path)
-}
-
 // ---------------------------------------------------------------- CTA-pair attention
-// The same algorithm on a cluster of two CTAs (two SMs) sharing each MMA (tcgen05 cta_group::2):
-// a pair covers 2 x 256 query rows of one (batch, head); query tile t of the pair is 256 rows, 128
-// in each CTA's shared memory and TMEM. For QK the pair's 128-key K tile is split by key (64 keys
-// in each CTA); for PV the V tile is split by head dimension (64 columns in each CTA). Each CTA
-// therefore streams half the K/V bytes through its shared memory per MMA, which lifts the
-// shared-memory bandwidth limit of the one-CTA QK MMA (A 4 KB + B 4 KB per 64 cycles).
+// A cluster of two CTAs (two SMs) shares each MMA (tcgen05 cta_group::2): a pair covers 2 x 256
+// query rows of one (batch, head); query tile t of the pair is 256 rows, 128 in each CTA's shared
+// memory and TMEM. For QK the pair's 128-key K tile is split by key (64 keys in each CTA); for PV
+// the V tile is split by head dimension (64 columns in each CTA). Each CTA therefore streams half
+// the K/V bytes through its shared memory per MMA (A 4 KB + B 2 KB per 64 cycles, where a one-CTA
+// M=128 MMA would need A 4 KB + B 4 KB and meet the shared-memory operand bandwidth).
 // The even CTA issues every MMA; both CTAs run producers and softmax warpgroups. Operand loads
 // complete on the leader's barriers (cta_group::2 tile loads, no multicast), MMA completion is
 // committed to both CTAs, and the peer's softmax warps arrive on the leader's P barriers.
@@ -487,7 +296,6 @@ __device__ __forceinline__ void issue_pv_pair_half(uint32_t d_o, uint32_t p_tmem
   }
 }
 
-template <int kPoly>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cm_attend_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -605,8 +413,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_commit_pair(&bars[O_FULL]);
     }
   } else {
-    softmax_role<kPoly, true, true>(p, bars, abort_flag, tbase, warp, lane, q_base, 2 * kTile, bh, n_tiles,
-                                    lead_bars + P_FULL * 8);
+    softmax_role(p, bars, abort_flag, tbase, warp, lane, q_base, 2 * kTile, bh, n_tiles, lead_bars + P_FULL * 8);
   }
 
   tc_fence_before();
@@ -757,10 +564,12 @@ int vomni::cm_attend_gated(const void* q, const void* k, const void* v, int b, i
   if (q_stride == 0) q_stride = static_cast<long long>(row_elems);
   if (kv_stride == 0) kv_stride = static_cast<long long>(row_elems);
   if (q_stride < static_cast<long long>(row_elems) || kv_stride < static_cast<long long>(row_elems)) return VOMNI_EBADSHAPE;
+  // Q and V: [64 dims x 128 rows] boxes; K: [64 dims x 64 keys] boxes (each CTA of a pair loads half
+  // of a 128-key tile).
   CUtensorMap tq, tk, tv;
   rc = make_tmap_3d_bf16(&tq, q, row_elems, s_q, b, 64, 128, static_cast<uint64_t>(q_stride));
   if (rc) return rc;
-  rc = make_tmap_3d_bf16(&tk, k, row_elems, s_kv, b, 64, 128, static_cast<uint64_t>(kv_stride));
+  rc = make_tmap_3d_bf16(&tk, k, row_elems, s_kv, b, 64, 64, static_cast<uint64_t>(kv_stride));
   if (rc) return rc;
   rc = make_tmap_3d_bf16(&tv, v, row_elems, s_kv, b, 64, 128, static_cast<uint64_t>(kv_stride));
   if (rc) return rc;
@@ -783,57 +592,20 @@ int vomni::cm_attend_gated(const void* q, const void* k, const void* v, int b, i
   p.ready = ready;
   p.ready_epoch = ready_epoch;
 
-  // Tuning knobs (read once): VOMNI_CM_POLY = share of exponentials on the FMA pipe as 1/N
-  // (0 = none), VOMNI_CM_SPLIT = 1 to publish P in two key halves, 0 for whole tiles,
-  // VOMNI_CM_PAIR = 1 for the CTA-pair kernel.
-  static int poly = -1, split = -1, pair = -1;
-  if (poly < 0) {
-    const char* e = getenv("VOMNI_CM_POLY");
-    poly = e ? atoi(e) : 0;
-    const char* f = getenv("VOMNI_CM_SPLIT");
-    split = f ? atoi(f) : 1;
-    const char* g = getenv("VOMNI_CM_PAIR");
-    pair = g ? atoi(g) : 1;
-  }
-  if (pair) {
-    CUtensorMap tk2;
-    rc = make_tmap_3d_bf16(&tk2, k, row_elems, s_kv, b, 64, 64, static_cast<uint64_t>(kv_stride));
-    if (rc) return rc;
-    auto pk = poly == 8 ? cm::cm_attend_pair_kernel<8> : cm::cm_attend_pair_kernel<0>;
-    rc = ensure_max_smem(pk, cm::kPairSmemBytes);
-    if (rc) return rc;
-    const int pairs = (s_q + 4 * cm::kTile - 1) / (4 * cm::kTile);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs, b * h);
-    cfg.blockDim = dim3(cm::kThreads);
-    cfg.dynamicSmemBytes = cm::kPairSmemBytes;
-    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = (flags & VOMNI_CM_OVERLAP) ? 1 : 0;
-    VOMNI_CUDA_TRY(cudaLaunchKernelEx(&cfg, pk, tq, tk2, tv, p));
-    return VOMNI_OK;
-  }
-  auto kern = cm::cm_attend_kernel<0, false>;
-  if (poly == 2) kern = split ? cm::cm_attend_kernel<2, true> : cm::cm_attend_kernel<2, false>;
-  else if (poly == 4) kern = split ? cm::cm_attend_kernel<4, true> : cm::cm_attend_kernel<4, false>;
-  else if (poly == 8) kern = split ? cm::cm_attend_kernel<8, true> : cm::cm_attend_kernel<8, false>;
-  else kern = split ? cm::cm_attend_kernel<0, true> : cm::cm_attend_kernel<0, false>;
-  rc = ensure_max_smem(kern, cm::kSmemBytes);
+  rc = ensure_max_smem(cm::cm_attend_pair_kernel, cm::kPairSmemBytes);
   if (rc) return rc;
+  const int pairs = (s_q + 4 * cm::kTile - 1) / (4 * cm::kTile);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((s_q + cm::kTile * cm::kQT - 1) / (cm::kTile * cm::kQT), b * h);
+  cfg.gridDim = dim3(2 * pairs, b * h);
   cfg.blockDim = dim3(cm::kThreads);
-  cfg.dynamicSmemBytes = cm::kSmemBytes;
+  cfg.dynamicSmemBytes = cm::kPairSmemBytes;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (flags & VOMNI_CM_OVERLAP) ? 1 : 0;
-  VOMNI_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, p));
+  VOMNI_CUDA_TRY(cudaLaunchKernelEx(&cfg, cm::cm_attend_pair_kernel, tq, tk, tv, p));
   return VOMNI_OK;
 }
 
@@ -887,6 +659,32 @@ extern "C" int vomni_cm_attention_local(const void* q, const void* k, const void
                                           workspace_bytes, stream);
 }
 
+// ---------------------------------------------------------------- exp2 self-test
+namespace vomni {
+namespace cm {
+__global__ void exp2_poly_selftest_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  const long long i = 2 * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  float p0, p1;
+  exp2_poly2(x[i], i + 1 < n ? x[i + 1] : 0.f, p0, p1);
+  y[i] = p0;
+  if (i + 1 < n) y[i + 1] = p1;
+}
+}  // namespace cm
+}  // namespace vomni
+
+extern "C" int vomni_selftest_exp2_poly(const float* x, float* y, long long n, vomni_stream_t stream) {
+  if (!x || !y) return VOMNI_EINVAL;
+  if (n <= 0 || n > (1ll << 40)) return VOMNI_EBADSHAPE;
+  const int threads = 256;
+  const long long blocks = ((n + 1) / 2 + threads - 1) / threads;
+  if (blocks > 0x7fffffffll) return VOMNI_EBADSHAPE;
+  cm::exp2_poly_selftest_kernel<<<static_cast<unsigned>(blocks), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, y, n);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
 // ---------------------------------------------------------------- allocation-free variant
 // Some callers cannot allocate device memory: a plugin inside a host runtime that owns the whole
 // device heap (an inference server's pool, a C plugin ABI with no allocator hook), or a
@@ -898,22 +696,57 @@ static __device__ __align__(256) unsigned char g_cm_noalloc_scratch[kNoAllocScra
 
 namespace {
 constexpr int kNoAllocMaxDevices = 64;
-void* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+struct NoAllocSlot {
+  unsigned long long ctx_id;  // driver context the address belongs to (0: not resolved yet)
+  void* ptr;
+};
+NoAllocSlot g_noalloc_slot[kNoAllocMaxDevices] = {};
 std::mutex g_noalloc_mu;
 
-// Device address of the scratch array on the current device. The array's name is only a host-side
-// stand-in, so the address is looked up once per device (with that device current) and cached.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current driver context (0 if none or unavailable). A device
+// reset (cudaDeviceReset) destroys the primary context and the next runtime call creates a new one
+// with a new id, so an address cached under the old id is never reused.
+unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of the scratch array on the current device. In host code the array's name is only
+// a host-side stand-in, so the address is looked up with cudaGetSymbolAddress, with the device
+// current, the first time a device (or a device's new context after a reset) is seen, and cached.
 int noalloc_scratch(void** out) {
   int dev = 0;
   VOMNI_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kNoAllocMaxDevices) return VOMNI_ENOTSUP;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_scratch_ptr[dev]) {
+  NoAllocSlot& slot = g_noalloc_slot[dev];
+  const unsigned long long id = current_ctx_id();
+  if (!slot.ptr || id == 0 || id != slot.ctx_id) {
     void* p = nullptr;
     VOMNI_CUDA_TRY(cudaGetSymbolAddress(&p, g_cm_noalloc_scratch));
-    g_noalloc_scratch_ptr[dev] = p;
+    slot.ptr = p;
+    slot.ctx_id = current_ctx_id();  // the lookup makes the runtime's context current if it was not
   }
-  *out = g_noalloc_scratch_ptr[dev];
+  *out = slot.ptr;
   return VOMNI_OK;
 }
 }  // namespace

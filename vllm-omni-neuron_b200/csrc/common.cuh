@@ -351,22 +351,60 @@ VOMNI_DEV float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA pipe, for x <= 0 (softmax exponents under a fixed upper bound). Cody-Waite split
-// x = n + f with n = rint(x) (added to 1.5 * 2^23 so n lands in the low mantissa bits) and
-// f in [-0.5, 0.5]; 2^f from a degree-3 polynomial whose coefficients come from a Remez exchange
-// minimising the relative error on [-0.5, 0.5] (max 7.5e-5, i.e. 2^-13.7, far below the bf16
-// rounding the result gets); 2^n is then added into the exponent field. x is clamped at -125 so
-// the exponent never underflows: inputs below give 2^-125 (~2.4e-38) instead of 0.
-VOMNI_DEV float exp2_poly(float x) {
-  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
-  x = fmaxf(x, -125.f);
-  const float t = x + kRound;
-  const float f = x - (t - kRound);
-  float p = fmaf(0.0551716685f, f, 0.2426111251f);
-  p = fmaf(p, f, 0.6932609677f);
-  p = fmaf(p, f, 0.9999280572f);
-  // (bits(t) - bits(kRound)) << 23 == bits(t) << 23 (mod 2^32): bits(kRound) has 23 zero low bits.
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+
+// Packed fp32 pairs (sm_100 `.f32x2` arithmetic): one instruction operates on two fp32 values held
+// in a 64-bit register pair, halving the issue slots of elementwise fp32 work. Each lane of the
+// pair is rounded exactly as the scalar instruction would round it.
+VOMNI_DEV uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+VOMNI_DEV void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+VOMNI_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+VOMNI_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+VOMNI_DEV uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// 2^x for a pair of fp32 values on the FMA pipe, so that a share of the softmax exponentials
+// bypasses the MUFU unit (which delivers 16 results per clock per SM, the same rate as the tensor
+// pipe needs them at head dim 128). Method: Cody-Waite range reduction x = n + f with n = rint(x),
+// obtained by adding 1.5 * 2^23 so that n lands in the low mantissa bits, and f in [-0.5, 0.5];
+// 2^f from a degree-3 polynomial whose coefficients were fitted by a Remez exchange minimising the
+// relative error on [-0.5, 0.5] (max 7.5e-5 = 2^-13.7, far below the bf16 rounding that softmax
+// probabilities get); 2^n is added into the exponent field as an integer. That addition is exact
+// while the result stays a normal number (n >= -125); below x = -125.5 the result is 0, as the
+// flush-to-zero MUFU exponential gives 0 for results under 2^-126. The reduction and the polynomial
+// run as `.f32x2` pairs (6 instructions for two values).
+constexpr float kExp2Round = 12582912.f;  // 1.5 * 2^23
+constexpr float kExp2C3 = 0.0551716685f, kExp2C2 = 0.2426111251f, kExp2C1 = 0.6932609677f, kExp2C0 = 0.9999280572f;
+VOMNI_DEV void exp2_poly2(float x0, float x1, float& p0, float& p1) {
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t rnd = f2_pack(kExp2Round, kExp2Round);
+  const uint64_t t = f2_add(x, rnd);
+  const uint64_t f = f2_sub(x, f2_sub(t, rnd));
+  uint64_t p = f2_fma(f2_pack(kExp2C3, kExp2C3), f, f2_pack(kExp2C2, kExp2C2));
+  p = f2_fma(p, f, f2_pack(kExp2C1, kExp2C1));
+  p = f2_fma(p, f, f2_pack(kExp2C0, kExp2C0));
+  float plo, phi, tlo, thi;
+  f2_unpack(p, plo, phi);
+  f2_unpack(t, tlo, thi);
+  // (bits(t) - bits(1.5 * 2^23)) << 23 == n << 23 (mod 2^32): the constant's 23 low bits are 0.
+  const float r0 = __int_as_float(__float_as_int(plo) + (__float_as_int(tlo) << 23));
+  const float r1 = __int_as_float(__float_as_int(phi) + (__float_as_int(thi) << 23));
+  p0 = x0 > -125.5f ? r0 : 0.f;
+  p1 = x1 > -125.5f ? r1 : 0.f;
 }
 // Two fp32 -> packed bf16x2 (round to nearest even); `lo` lands in bits 0-15.
 VOMNI_DEV uint32_t pack_bf16x2(float lo, float hi) {
