@@ -31,17 +31,11 @@ def test_phase_plan_covers_each_block_once(ring, world):
     assert slots == list(range(world - 1))
 
 
-def test_phase_plan_knob(ring, monkeypatch):
-    """VOMNI_RING_PLAN replaces the doubling pass sizes; the last size repeats; bad values are refused."""
-    monkeypatch.setenv("VOMNI_RING_PLAN", "2,5")
-    assert ring.phase_plan(8) == [(-1, 1), (0, 2), (2, 5)]
-    monkeypatch.setenv("VOMNI_RING_PLAN", "3")
-    assert ring.phase_plan(8) == [(-1, 1), (0, 3), (3, 3), (6, 1)]
-    monkeypatch.setenv("VOMNI_RING_PLAN", "0")
-    with pytest.raises(Exception):
-        ring.phase_plan(8)
-    monkeypatch.delenv("VOMNI_RING_PLAN")
+def test_phase_plan_default(ring):
+    """The pass sizes double after the local pass: 1, 2, 4, ... (the last pass takes the remainder)."""
     assert ring.phase_plan(8) == [(-1, 1), (0, 1), (1, 2), (3, 4)]
+    assert ring.phase_plan(4) == [(-1, 1), (0, 1), (1, 2)]
+    assert ring.phase_plan(1) == [(-1, 1)]
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])

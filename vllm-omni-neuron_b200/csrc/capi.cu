@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <tuple>
@@ -21,9 +22,11 @@ namespace vomni {
 namespace {
 thread_local cudaError_t g_last_cuda_error = cudaSuccess;
 constexpr int kMaxDevices = 64;
-int* g_status_ptr[kMaxDevices] = {};
-int g_num_sms[kMaxDevices] = {};
-int g_is_sm100[kMaxDevices] = {};  // 0 unknown, 1 yes, -1 no
+// Per-device caches, filled on first use by whichever host thread gets there first (every writer
+// stores the same value), read lock-free afterwards.
+std::atomic<int*> g_status_ptr[kMaxDevices] = {};
+std::atomic<int> g_num_sms[kMaxDevices] = {};
+std::atomic<int> g_is_sm100[kMaxDevices] = {};  // 0 unknown, 1 yes, -1 no
 std::mutex g_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -39,42 +42,47 @@ void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = e; }
 int num_sms() {
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return 148;
-  if (!g_num_sms[dev]) {
-    int n = 0;
+  int n = g_num_sms[dev].load(std::memory_order_acquire);
+  if (!n) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_num_sms[dev] = n;
+    g_num_sms[dev].store(n, std::memory_order_release);
   }
-  return g_num_sms[dev];
+  return n;
 }
 
 int require_sm100() {
   const int dev = current_device();
   if (dev < 0) return VOMNI_ECUDA;
-  if (dev < kMaxDevices && g_is_sm100[dev]) return g_is_sm100[dev] > 0 ? VOMNI_OK : VOMNI_ENOTSUP;
+  if (dev < kMaxDevices) {
+    const int known = g_is_sm100[dev].load(std::memory_order_acquire);
+    if (known) return known > 0 ? VOMNI_OK : VOMNI_ENOTSUP;
+  }
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return VOMNI_ECUDA;
   if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return VOMNI_ECUDA;
   const bool ok = (major == 10 && minor == 0);
-  if (dev < kMaxDevices) g_is_sm100[dev] = ok ? 1 : -1;
+  if (dev < kMaxDevices) g_is_sm100[dev].store(ok ? 1 : -1, std::memory_order_release);
   return ok ? VOMNI_OK : VOMNI_ENOTSUP;
 }
 
 int* device_status_ptr() {
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return nullptr;
-  if (!g_status_ptr[dev]) {
+  int* ptr = g_status_ptr[dev].load(std::memory_order_acquire);
+  if (!ptr) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_status_ptr[dev]) {
+    ptr = g_status_ptr[dev].load(std::memory_order_relaxed);
+    if (!ptr) {
       void* p = nullptr;
       if (cudaGetSymbolAddress(&p, g_vomni_status) != cudaSuccess) return nullptr;
-      g_status_ptr[dev] = static_cast<int*>(p);
+      ptr = static_cast<int*>(p);
+      g_status_ptr[dev].store(ptr, std::memory_order_release);
     }
   }
-  return g_status_ptr[dev];
+  return ptr;
 }
 
 static int get_encoder() {
-  if (g_encode) return VOMNI_OK;
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_encode) return VOMNI_OK;
   void* fn = nullptr;

@@ -11,11 +11,12 @@
 //          out = x*inv*cos + [-x_hi, x_lo]*inv*sin                  (_rope_segment, :4069-4114)
 // The MX engine's identity micro-scales (common_types.py:77-78) make the ROW mode a plain FP8 GEMM.
 //
-// GEMM kernel: persistent, one CTA per SM walking 128 x 256 output tiles; warp 0 TMA producer
-// (A [128 x 128 B] and B [256 x 128 B] boxes, 128-byte swizzle, 4-stage ring), warp 1 TMEM owner +
-// tcgen05.mma kind::f8f6f4 issuer (M=128, N=256, K=32 per instruction) into one of two 256-column
-// accumulators, warps 2-5 epilogue (TMEM -> registers, scales + bias, bf16 stores, per-row partial
-// sums of squares) on the other accumulator.
+// GEMM kernels: persistent clusters of two CTAs (tcgen05 cta_group::2) walking 256 x 256 output
+// tiles; per CTA warp 0 is the TMA producer (its 128 rows of A and 128 rows of W per 128-byte
+// k-block, 128-byte swizzle, 6-stage ring), warp 1 the TMEM owner and, in the even CTA, the
+// tcgen05.mma issuer (M=256, N=256, K=32 per instruction) into one of two 256-column accumulators,
+// and the remaining warps the epilogue (TMEM -> registers, scales + bias, bf16 stores, per-row
+// partial sums of squares) on the other accumulator.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -29,14 +30,7 @@ namespace vomni {
 namespace qkv {
 
 constexpr int kBM = 128, kBN = 256, kBK = 128;  // kBK in bytes (= fp8 elements)
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
-constexpr uint32_t kABytes = kBM * kBK;  // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK;  // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kSmemBar = kStages * kStageBytes;
-constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;
-constexpr uint32_t kIdesc = idesc_e4m3(kBM, kBN);
 constexpr uint32_t kSfAtomBytes = 512;  // one tcgen05 scale atom: 128 rows x 4 k-sub-blocks
 
 struct Params {
@@ -59,181 +53,6 @@ struct Params {
 // Epilogues of the ROW GEMM: bf16 Y + per-head sums of squares (QKV), or bias + GELU-tanh + MX-32
 // quantisation of the result (the ROW_MX MLP's up-projection).
 enum { EPI_QKV = 0, EPI_MX_GELU = 1 };
-
-// Persistent: CTA c processes tiles c, c + gridDim.x, ... (n fastest, so the CTAs in flight share
-// the A rows and walk the whole weight, which stays L2-resident). The two 256-column TMEM
-// accumulators alternate between tiles, so the epilogue of tile i overlaps the main loop of i+1.
-__global__ void __launch_bounds__(kThreads, 1)
-    qkv_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmemBar);
-  uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;   // [2]
-  uint64_t* acc_empty = acc_full + 2;     // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nk = p.H / kBK;
-  const int n_all = p.m_tiles * p.n_tiles;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * kBN);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmA);
-      tma_prefetch_desc(&tmB);
-      uint32_t it = 0;  // global k-block counter across this CTA's tiles (stage ring position)
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x) {
-        const int m0 = (tile / p.n_tiles) * kBM;
-        const int n0 = (tile % p.n_tiles) * kBN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int st = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
-          if (it >= kStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sa = smem + st * kStageBytes;
-          mbar_expect_tx(&full[st], kStageBytes);
-          tma_load_2d(&tmA, &full[st], sa, kb * kBK, m0);
-          tma_load_2d(&tmB, &full[st], sa + kABytes, kb * kBK, n0);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128);
-      uint32_t it = 0;
-      int lt = 0;  // local tile index
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x, ++lt) {
-        const int acc = lt & 1;
-        if (lt >= 2 && !mbar_wait(&acc_empty[acc], ((lt >> 1) & 1) ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24)) break;
-        tc_fence_after();
-        const uint32_t tacc = tbase + acc * kBN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int st = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x22)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // Start-address field advanced by integer adds (address >> 4; no carry below 256 KB).
-          const uint64_t ad0 = a_desc0 + ((st * kStageBytes) >> 4);
-          const uint64_t bd0 = ad0 + (kABytes >> 4);
-#pragma unroll
-          for (int k4 = 0; k4 < kBK / 32; ++k4)
-            mma_f8_ss(tacc, ad0 + k4 * 2, bd0 + k4 * 2, kIdesc, (kb > 0 || k4 > 0) ? 1u : 0u);
-          tc_commit(&empty[st]);
-        }
-        if (ok) tc_commit(&acc_full[acc]);
-      }
-    }
-  } else {
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
-    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    int lt = 0;
-    for (int tile = blockIdx.x; tile < n_all; tile += gridDim.x, ++lt) {
-      const int acc = lt & 1;
-      if (!mbar_wait(&acc_full[acc], (lt >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x23)) break;
-      tc_fence_after();
-      const int m0 = (tile / p.n_tiles) * kBM;
-      const int nt = tile % p.n_tiles;
-      const int n0 = nt * kBN;
-      const int grow = m0 + row;
-      const bool row_ok = grow < p.T;
-      const uint32_t tacc = tbase + lane_addr + acc * kBN;
-      const float rs = row_ok ? p.row_scale[grow] : 0.f;
-      float ss = 0.f, ss_lo = 0.f;
-      __nv_bfloat16* yrow = p.y + static_cast<size_t>(grow) * p.I + n0;
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tacc + c * 32, r);
-        tmem_ld_wait(r);
-        const int col0 = n0 + c * 32;
-        const float4* cs4 = reinterpret_cast<const float4*>(p.chan_scale + col0);
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 cs = cs4[i];
-          v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) * rs * cs.x;
-          v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) * rs * cs.y;
-          v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * rs * cs.z;
-          v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * rs * cs.w;
-        }
-        if (p.bias) {
-          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 bb = b4[i];
-            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(b2[j]);
-              v[8 * i + 2 * j] += f.x;
-              v[8 * i + 2 * j + 1] += f.y;
-            }
-          }
-        }
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-          const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
-          ss = fmaf(lo, lo, fmaf(hi, hi, ss));
-        }
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(yrow + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-        }
-        if (c == 3) {  // first 128 columns (one head) done
-          ss_lo = ss;
-          ss = 0.f;
-        }
-      }
-      // The accumulator has been read: the MMA warp may reuse it for tile lt + 2.
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
-      if (row_ok && p.sumsq && 2 * nt < p.n_norm_heads) {
-        float* dst = p.sumsq + static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt;
-        dst[0] = ss_lo;
-        dst[1] = ss;
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tbase, 2 * kBN);
-  }
-}
 
 // ---------------------------------------------------------------- ROW mode on CTA pairs
 // The same GEMM on a cluster of two CTAs sharing each MMA (tcgen05 cta_group::2, M=256): a pair
@@ -540,14 +359,8 @@ __global__ void mx_pack_scales_kernel(const uint8_t* __restrict__ sf, int rows, 
   out[idx] = r < rows ? sf[static_cast<size_t>(r) * kblk32 + kb * 4 + j] : static_cast<uint8_t>(127);
 }
 
-constexpr int kMxStages = 4;
 constexpr uint32_t kMxSfaBytes = kSfAtomBytes;      // 128 rows of A
 constexpr uint32_t kMxSfbBytes = 2 * kSfAtomBytes;  // 256 rows of B
-// Stage = A tile, B tile, then the scale atoms, padded to 1 KB so every stage's A/B tiles keep the
-// 1024-byte alignment the 128-byte swizzle pattern is defined on.
-constexpr uint32_t kMxStageBytes = (kABytes + kBBytes + kMxSfaBytes + kMxSfbBytes + 1023) / 1024 * 1024;
-constexpr uint32_t kMxSmemBar = kMxStages * kMxStageBytes;
-constexpr uint32_t kMxSmemBytes = kMxSmemBar + 256 + 1024;
 constexpr uint32_t kMxColSf = kBN;  // scale columns follow the single accumulator: 12 per stage
 
 struct MxParams {
@@ -579,177 +392,7 @@ VOMNI_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* ba
                : "memory");
 }
 
-// Persistent like the ROW kernel, with one 256-column accumulator (TMEM also holds the staged
-// scale factors); the epilogue releases the accumulator as soon as it sits in registers.
 constexpr int kMxThreads = 320;  // TMA warp, MMA warp, eight epilogue warps
-
-__global__ void __launch_bounds__(kMxThreads, 1)
-    qkv_gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const MxParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kMxSmemBar);
-  uint64_t* empty = full + kMxStages;
-  uint64_t* acc_full = empty + kMxStages;
-  uint64_t* acc_empty = acc_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nk = p.H / kBK;
-  const int n_all = p.m_tiles * p.n_tiles;
-  const int n128 = p.I / 128;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kMxStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 256);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmA);
-      tma_prefetch_desc(&tmB);
-      uint32_t it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x) {
-        const int mb = tile / p.n_tiles;
-        const int nb = tile % p.n_tiles;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int st = it % kMxStages;
-          const uint32_t ph = (it / kMxStages) & 1;
-          if (it >= kMxStages && !mbar_wait(&empty[st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x41)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sa = smem + st * kMxStageBytes;
-          mbar_expect_tx(&full[st], kABytes + kBBytes + kMxSfaBytes + kMxSfbBytes);
-          tma_load_2d(&tmA, &full[st], sa, kb * kBK, mb * kBM);
-          tma_load_2d(&tmB, &full[st], sa + kABytes, kb * kBK, nb * kBN);
-          bulk_g2s(sa + kABytes + kBBytes, p.sfa + (static_cast<size_t>(kb) * p.m_tiles + mb) * kSfAtomBytes,
-                   kMxSfaBytes, &full[st]);
-          bulk_g2s(sa + kABytes + kBBytes + kMxSfaBytes,
-                   p.sfb + (static_cast<size_t>(kb) * n128 + nb * 2) * kSfAtomBytes, kMxSfbBytes, &full[st]);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint64_t a_desc0 = make_sdesc(smem_u32(smem), 16, 1024, kLayoutSW128);
-      // scale atoms: 32 rows of 16 bytes, no swizzle; 8-row core matrices 128 B apart
-      const uint64_t sf_desc0 = make_sdesc(smem_u32(smem + kABytes + kBBytes), 16, 128, 0);
-      uint32_t it = 0;
-      int lt = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_all; tile += gridDim.x, ++lt) {
-        if (lt >= 1 && !mbar_wait(acc_empty, (lt - 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x44)) break;
-        tc_fence_after();
-        for (int kb = 0; kb < nk; ++kb, ++it) {
-          const int st = it % kMxStages;
-          const uint32_t ph = (it / kMxStages) & 1;
-          if (!mbar_wait(&full[st], ph, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x42)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t sdesc = sf_desc0 + ((st * kMxStageBytes) >> 4);
-          const uint32_t t_sfa = tbase + kMxColSf + st * 12;
-          const uint32_t t_sfb = t_sfa + 4;
-          tmem_cp_32x128b_warpx4(t_sfa, sdesc);
-          tmem_cp_32x128b_warpx4(t_sfb, sdesc + (kMxSfaBytes >> 4));
-          tmem_cp_32x128b_warpx4(t_sfb + 4, sdesc + ((kMxSfaBytes + kSfAtomBytes) >> 4));
-          const uint64_t ad0 = a_desc0 + ((st * kMxStageBytes) >> 4);
-          const uint64_t bd0 = ad0 + (kABytes >> 4);
-#pragma unroll
-          for (int k4 = 0; k4 < kBK / 32; ++k4)
-            // the scale byte (k-block within the 128-wide stage) sits in both the instruction
-            // descriptor and bits 30-31 of the scale-factor TMEM addresses
-            mma_mxf8_ss(tbase, ad0 + k4 * 2, bd0 + k4 * 2, idesc_mxf8(kBM, kBN, k4), (kb > 0 || k4 > 0) ? 1u : 0u,
-                        t_sfa | (static_cast<uint32_t>(k4) << 30), t_sfb | (static_cast<uint32_t>(k4) << 30));
-          tc_commit(&empty[st]);
-        }
-        if (ok) tc_commit(acc_full);
-      }
-    }
-  } else {
-    // Eight epilogue warps: two per TMEM lane quadrant, each owning 128 of the 256 columns. A warp
-    // drains its half of the accumulator into registers (bias added, rounded to bf16), releases the
-    // accumulator to the MMA warp, and only then stores, so the stores overlap the next tile's MMAs.
-    const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int row = quad * 32 + lane;
-    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    int lt = 0;
-    for (int tile = blockIdx.x; tile < n_all; tile += gridDim.x, ++lt) {
-      if (!mbar_wait(acc_full, lt & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x43)) break;
-      tc_fence_after();
-      const int m0 = (tile / p.n_tiles) * kBM;
-      const int nt = tile % p.n_tiles;
-      const int n0 = nt * kBN + half * 128;
-      const int grow = m0 + row;
-      uint32_t pk[64];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + lane_addr + half * 128 + c * 32, r);
-        tmem_ld_wait(r);
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if (p.bias) {
-          const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0 + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 bb = b4[i];
-            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(b2[j]);
-              v[8 * i + 2 * j] += f.x;
-              v[8 * i + 2 * j + 1] += f.y;
-            }
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-      }
-      tc_fence_before();
-      mbar_arrive(acc_empty);
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float lo = __uint_as_float(pk[i] << 16), hi = __uint_as_float(pk[i] & 0xFFFF0000u);
-        ss = fmaf(lo, lo, fmaf(hi, hi, ss));
-      }
-      if (grow < p.T) {
-        uint4* dst = reinterpret_cast<uint4*>(p.y + static_cast<size_t>(grow) * p.I + n0);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-      }
-      if (p.sumsq && grow < p.T && 2 * nt + half < p.n_norm_heads)
-        p.sumsq[static_cast<size_t>(grow) * p.n_norm_heads + 2 * nt + half] = ss;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tbase, 512);
-  }
-}
 
 // MX-32 on CTA pairs: 256 x 256 pair tiles, cta_group::2 block-scaled MMA (M=256, N=256, K=32).
 // Each CTA stages its 128 rows of X, its 128 rows of W, the scale atom of its X rows and the two
@@ -758,6 +401,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 constexpr int kMxPairStages = 6;
 constexpr uint32_t kMxPairABytes = kBM * kBK;  // 16 KB
 constexpr uint32_t kMxPairBBytes = 128 * kBK;  // 16 KB
+// Stage = A tile, B tile, then the scale atoms, padded to 1 KB so every stage's A/B tiles keep the
+// 1024-byte alignment the 128-byte swizzle pattern is defined on.
 constexpr uint32_t kMxPairStageBytes =
     (kMxPairABytes + kMxPairBBytes + kMxSfaBytes + kMxSfbBytes + 1023) / 1024 * 1024;  // 34 KB
 constexpr uint32_t kMxPairTx = kMxPairABytes + kMxPairBBytes + kMxSfaBytes + kMxSfbBytes;
@@ -1112,10 +757,12 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
   if (static_cast<long long>(t + qkv::kBM - 1) / qkv::kBM > 0x7fffffffLL) return VOMNI_EBADSHAPE;
   int rc = require_sm100();
   if (rc) return rc;
+  // X: [128 B x 128 rows] boxes; W: [128 B x 128 rows] boxes (each CTA of a pair loads half of the
+  // 256 output columns).
   CUtensorMap ta, tb;
   rc = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_codes, h, t, h, qkv::kBK, qkv::kBM);
   if (rc) return rc;
-  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, qkv::kBN);
+  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
   if (rc) return rc;
   qkv::Params p;
   p.T = t;
@@ -1133,27 +780,12 @@ extern "C" int vomni_qkv_fp8_gemm(const void* x_codes, const float* row_scale, c
   p.codes = nullptr;
   p.sf = nullptr;
   p.sf_row_blocks = 0;
-  static const int use_pair = [] {
-    const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
-    return e ? atoi(e) : 1;
-  }();
-  rc = use_pair ? ensure_max_smem(qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV>, qkv::kPairSmemBytes)
-                : ensure_max_smem(qkv::qkv_gemm_kernel, qkv::kSmemBytes);
+  rc = ensure_max_smem(qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV>, qkv::kPairSmemBytes);
   if (rc) return rc;
-  if (use_pair) {
-    CUtensorMap tb2;
-    rc = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
-    if (rc) return rc;
-    const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
-    const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
-    qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV><<<2 * pairs, qkv::kThreads, qkv::kPairSmemBytes,
-                                              reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb2, p);
-    VOMNI_CUDA_TRY(cudaGetLastError());
-    return VOMNI_OK;
-  }
-  const int n_all = p.m_tiles * p.n_tiles;
-  const int grid = n_all < num_sms() ? n_all : num_sms();
-  qkv::qkv_gemm_kernel<<<grid, qkv::kThreads, qkv::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
+  const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
+  qkv::qkv_gemm_pair_kernel<qkv::EPI_QKV><<<2 * pairs, qkv::kThreads, qkv::kPairSmemBytes,
+                                            reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }
@@ -1208,7 +840,7 @@ extern "C" int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed,
   CUtensorMap ta, tb;
   rc = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_codes, h, t, h, qkv::kBK, qkv::kBM);
   if (rc) return rc;
-  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, qkv::kBN);
+  rc = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
   if (rc) return rc;
   qkv::MxParams p;
   p.T = t;
@@ -1227,33 +859,19 @@ extern "C" int vomni_qkv_mx32_gemm(const void* x_codes, const void* x_sf_packed,
   p.residual = nullptr;
   p.gate = nullptr;
   p.gate_rows = 1;
-  static const int use_pair = [] {
-    const char* e = getenv("VOMNI_QKV_PAIR");  // 1 (default): CTA-pair kernel; 0: one-CTA kernel
-    return e ? atoi(e) : 1;
-  }();
-  rc = use_pair ? ensure_max_smem(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV>, qkv::kMxPairSmemBytes)
-                : ensure_max_smem(qkv::qkv_gemm_mx_kernel, qkv::kMxSmemBytes);
+  rc = ensure_max_smem(qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV>, qkv::kMxPairSmemBytes);
   if (rc) return rc;
-  if (use_pair) {
-    // X scale atoms must exist for every 128-row block a pair tile touches (pair bands are 256 rows)
-    CUtensorMap tb2, tsa, tsb;
-    rc = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, h, i, h, qkv::kBK, 128);
-    if (rc) return rc;
-    const uint64_t k128 = static_cast<uint64_t>(h / 128);
-    rc = make_tmap_2d_plain(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_sf_packed, 128, k128 * p.m_tiles * 4, 128, 128, 4);
-    if (rc) return rc;
-    rc = make_tmap_2d_plain(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_sf_packed, 128, k128 * (i / 128) * 4, 128, 128, 8);
-    if (rc) return rc;
-    const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
-    const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
-    qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV><<<2 * pairs, qkv::kMxThreads, qkv::kMxPairSmemBytes,
-                                                    reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb2, tsa, tsb, p);
-    VOMNI_CUDA_TRY(cudaGetLastError());
-    return VOMNI_OK;
-  }
-  const int n_all = p.m_tiles * p.n_tiles;
-  const int grid = n_all < num_sms() ? n_all : num_sms();
-  qkv::qkv_gemm_mx_kernel<<<grid, qkv::kMxThreads, qkv::kMxSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  // X scale atoms must exist for every 128-row block a pair tile touches (pair bands are 256 rows)
+  CUtensorMap tsa, tsb;
+  const uint64_t k128 = static_cast<uint64_t>(h / 128);
+  rc = make_tmap_2d_plain(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, x_sf_packed, 128, k128 * p.m_tiles * 4, 128, 128, 4);
+  if (rc) return rc;
+  rc = make_tmap_2d_plain(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_sf_packed, 128, k128 * (i / 128) * 4, 128, 128, 8);
+  if (rc) return rc;
+  const int pair_tiles = ((t + 255) / 256) * p.n_tiles;
+  const int pairs = pair_tiles < num_sms() / 2 ? pair_tiles : num_sms() / 2;
+  qkv::qkv_gemm_mx_pair_kernel<qkv::MX_EPI_QKV><<<2 * pairs, qkv::kMxThreads, qkv::kMxPairSmemBytes,
+                                                  reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, tsa, tsb, p);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }

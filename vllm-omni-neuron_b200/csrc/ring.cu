@@ -142,24 +142,12 @@ void ring_free(vomni_ring* R) {
 extern "C" int vomni_ring_phase_plan(int world, int* first, int* count, int max_phases) {
   // Pass 0 is the local block; passes 1.. cover gather slots [first, first+count) with counts
   // 1, 2, 4, ... (the last pass takes the remainder). Returns the number of passes.
-  // VOMNI_RING_PLAN="c1,c2,..." (tuning knob) replaces the doubling sizes; the last listed size
-  // repeats until all world - 1 slots are covered.
   if (world < 1 || !first || !count || max_phases < 1) return -VOMNI_EINVAL;
   int n = 0;
   first[n] = -1;
   count[n] = 1;
   ++n;
-  int sizes[16], n_sizes = 0;
-  if (const char* e = getenv("VOMNI_RING_PLAN")) {
-    while (*e && n_sizes < 16) {
-      const int c = atoi(e);
-      if (c < 1) return -VOMNI_EINVAL;
-      sizes[n_sizes++] = c;
-      while (*e && *e != ',') ++e;
-      if (*e == ',') ++e;
-    }
-  }
-  int slot = 0, size = n_sizes ? sizes[0] : 1, k = 0;
+  int slot = 0, size = 1;
   while (slot < world - 1) {
     if (n >= max_phases) return -VOMNI_EINVAL;
     const int c = (slot + size > world - 1) ? world - 1 - slot : size;
@@ -167,10 +155,7 @@ extern "C" int vomni_ring_phase_plan(int world, int* first, int* count, int max_
     count[n] = c;
     ++n;
     slot += c;
-    if (n_sizes)
-      size = sizes[++k < n_sizes ? k : n_sizes - 1];
-    else
-      size *= 2;
+    size *= 2;
   }
   return n;
 }
@@ -367,8 +352,17 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
     return VOMNI_ENCCL;
   }
   VOMNI_CUDA_TRY(cudaEventRecord(R->ev_ready, st));
-  // 4. direct pulls on the copy stream, in ring order
+  // 4. direct pulls on the copy stream, in ring order. A failure after the first copy is queued
+  //    leaves the ring unusable (peers' copies and ready words no longer match this call), so it
+  //    marks the ring broken; the caller stream still joins whatever was queued on the copy stream.
   VOMNI_CUDA_TRY(cudaStreamWaitEvent(R->copy_stream, R->ev_ready, 0));
+  auto pull_failed = [&](int status) {
+    R->broken = true;
+    if (cudaEventRecord(R->ev_copies_done, R->copy_stream) != cudaSuccess ||
+        cudaStreamWaitEvent(st, R->ev_copies_done, 0) != cudaSuccess)
+      cudaStreamSynchronize(R->copy_stream);  // cannot join by event: wait for the queued copies here
+    return status;
+  };
   const size_t gstride = static_cast<size_t>(N - 1) * s_loc * h * d * 2;  // per batch in the gather buffer
   for (int s = 1; s < N; ++s) {
     const int src = vomni_ring_source_rank(R->rank, N, s);
@@ -376,15 +370,29 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
     for (int bi = 0; bi < b; ++bi) {
       uint8_t* gk = static_cast<uint8_t*>(R->gather_k) + bi * gstride + static_cast<size_t>(s - 1) * blk;
       uint8_t* gv = static_cast<uint8_t*>(R->gather_v) + bi * gstride + static_cast<size_t>(s - 1) * blk;
-      VOMNI_CUDA_TRY(cudaMemcpyAsync(gk, ps + bi * bstride, blk, cudaMemcpyDeviceToDevice, R->copy_stream));
-      VOMNI_CUDA_TRY(cudaMemcpyAsync(gv, ps + R->block_bytes + bi * bstride, blk, cudaMemcpyDeviceToDevice, R->copy_stream));
+      cudaError_t e = cudaMemcpyAsync(gk, ps + bi * bstride, blk, cudaMemcpyDeviceToDevice, R->copy_stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(gv, ps + R->block_bytes + bi * bstride, blk, cudaMemcpyDeviceToDevice, R->copy_stream);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return pull_failed(VOMNI_ECUDA);
+      }
     }
-    VOMNI_CUDA_TRY(cudaEventRecord(R->ev_block[s], R->copy_stream));
+    const cudaError_t e = cudaEventRecord(R->ev_block[s], R->copy_stream);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return pull_failed(VOMNI_ECUDA);
+    }
     if (write_value && write_value(reinterpret_cast<CUstream>(R->copy_stream),
                                    reinterpret_cast<CUdeviceptr>(R->ready + s), epoch, 0) != CUDA_SUCCESS)
-      return VOMNI_ECUDA;
+      return pull_failed(VOMNI_ECUDA);
   }
-  VOMNI_CUDA_TRY(cudaEventRecord(R->ev_copies_done, R->copy_stream));
+  if (const cudaError_t e = cudaEventRecord(R->ev_copies_done, R->copy_stream); e != cudaSuccess) {
+    set_last_cuda_error(e);
+    R->broken = true;
+    cudaStreamSynchronize(R->copy_stream);
+    return VOMNI_ECUDA;
+  }
   // 5. passes: local block, then ranges of arrived blocks; fp32 partial, normalise on the last.
   // Every return from here joins the copy stream first (also on an error), so no later work on the
   // caller stream can overlap this call's copies.
