@@ -11,6 +11,8 @@ cannot run without a Trainium toolchain):
   adaln_quant_torch.py), loaded by file path;
 * ``_eager_adaln`` (diffusion/quantization/adaln_kernels.py:51-84), loaded by file path;
 * ``WanRotaryPosEmbed`` / ``apply_rotary_emb_wan`` (diffusion/layers/rope.py), by file path;
+* ``_mlp_ref_standard`` (kernels/nkilib/core/mlp/mlp_torch.py:401-600) in ROW_MX CTE mode, for the
+  ROW_MX MLP and, stopped after its up-projection, for the ROW_MX QKV dequant-matmul arithmetic;
 * ``build_fp8_dequant_mappings`` (diffusion/quantization/comfy_fp8_checkpoint.py, imported by path:
   it needs only the standard library) and ``dequantize_to_bf16`` (dequant_loaders.py:38-52, by ``ast``);
 * ``_torch_attend`` (diffusion/models/wan2_2/wan2_2_transformer.py:640-650), ``_wan_o_proj``
@@ -290,6 +292,88 @@ def gen_mlp_row_mx():
     np.savez_compressed(OUT / "mlp_row_mx.npz", **out)
 
 
+class _UpCaptured(Exception):
+    """Raised by the activation stand-in to stop _mlp_ref_standard right after the up-projection."""
+
+    def __init__(self, up):
+        super().__init__("captured")
+        self.up = up
+
+
+def gen_qkv_row_mx():
+    """The ROW_MX projection arithmetic on QKV-shaped operands, executed by the reference's own
+    ``_mlp_ref_standard`` (kernels/nkilib/core/mlp/mlp_torch.py:401-600) in ROW_MX CTE mode: its
+    up-projection ``(Xq * row_scale) @ (Wq * w_scale) + bias`` (fp32, :470-497 and :575-578) is the
+    same dequant-matmul as the ROW_MX QKV kernel's ``_dequant_row_mx`` (qkv_cte.py:3996-4021). The
+    activation stand-in captures ``up_out`` and stops the run there (the MLP's activation, MX
+    quantisation and down-projection are not part of the QKV path). Per-tensor Q/K/V weight scales
+    (row_mx_loaders.py:246-260) are passed through the ROW_MX ``[128, I/512, 4]`` scale layout that
+    the function un-permutes (:493-495). Stand-ins as in ``gen_mlp_row_mx``."""
+    ct_path = REF / "kernels/nkilib/core/utils/common_types.py"
+    from enum import Enum
+    from typing import Optional
+    env = {"Enum": Enum, "Optional": Optional}
+    enums = _extract(ct_path, ["ActFnType", "QuantizationType", "ComputationMode", "MLPGateUpWeightLayout"], env)
+    nl = types.SimpleNamespace(float8_e4m3fn="e4m3fn", float8_e4m3="e4m3", float8_e4m3fn_x4="e4m3fn_x4",
+                               float32=np.float32)
+    held = {}
+
+    def capture(x, fn):
+        raise _UpCaptured(x)
+
+    ident_w = lambda w, *a, **k: w  # noqa: E731
+    env = {
+        "torch": torch, "np": np, "math": math, "Optional": Optional, "nl": nl, **enums,
+        "_fp8_round_trip": lambda t, quant_dtype=None: t.to(torch.float8_e4m3fn).to(torch.float32),
+        "_extract_precomputed_row_scale": lambda hidden, H: (hidden[..., :H], held["row_scale"].reshape(-1, 1)),
+        "_apply_activation": capture,
+        "_undo_mx_gate_up_w_reshape": ident_w, "_undo_mx_down_w_reshape": ident_w,
+        "_undo_mx_gate_up_bias_reshape": ident_w, "_FP8_E4M3_MAX": 240.0, "_FP8_E4M3FN_MAX": 448.0,
+    }
+    mt = REF / "kernels/nkilib/core/mlp/mlp_torch.py"
+    fns = _extract(mt, ["_apply_clamp", "_is_tkg", "_mlp_ref_standard"], env)
+    QT, AF, CM, LY = (enums[n] for n in ("QuantizationType", "ActFnType", "ComputationMode", "MLPGateUpWeightLayout"))
+    rng = torch.Generator().manual_seed(20261206)
+    out = {}
+    # two shapes with 4 heads per segment (I = 1536, a multiple of the 512-column scale layout); the
+    # full config-3 width is covered by the GPU tests against the oracle this fixture pins
+    for tag, (T, H, heads) in {"a": (32, 1024, 4), "b": (40, 512, 4)}.items():
+        I = 3 * heads * 128
+        x = torch.randn(T, H, generator=rng)
+        rs = torch.clamp(x.abs().amax(1) / 448.0, min=1e-6)  # the adaLN ROW output (codes + per-row scale)
+        codes = (x * (1.0 / rs)[:, None]).to(torch.float8_e4m3fn)
+        w = torch.randn(H, I, generator=rng) * 0.02
+        seg = heads * 128
+        cs = torch.empty(I)
+        wc = torch.empty(H, I, dtype=torch.float8_e4m3fn)
+        for lo in (0, seg, 2 * seg):  # per-tensor Q, K, V scales
+            sc = float(w[:, lo:lo + seg].abs().max() / 448.0)
+            cs[lo:lo + seg] = sc
+            wc[:, lo:lo + seg] = (w[:, lo:lo + seg] / sc).to(torch.float8_e4m3fn)
+        bias = (0.1 * torch.randn(I, generator=rng)).to(torch.bfloat16)
+        held["row_scale"] = rs
+        hidden = torch.cat([codes.float(), torch.zeros(T, 4)], dim=1).unsqueeze(0)  # [1, T, H + 4]
+        up_scale = cs.reshape(I // 512, 128, 4).permute(1, 0, 2).contiguous()  # un-permuted by :493-495
+        try:
+            fns["_mlp_ref_standard"](
+                hidden=hidden, gate_w=wc.float(), up_w=wc.float(), down_w=torch.zeros(I, H),
+                quantization_type=QT.ROW_MX, gate_w_scale=None, up_w_scale=up_scale,
+                down_w_scale=torch.ones(128, H), gate_up_in_scale=None, down_in_scale=None,
+                quant_clipping_bound=None, gate_proj_bias_tensor=None,
+                up_proj_bias_tensor=bias.float().reshape(1, I), down_proj_bias_tensor=None, skip_gate_proj=True,
+                activation_fn=AF.GELU_Tanh_Approx, gate_clamp_upper_limit=None, gate_clamp_lower_limit=None,
+                up_clamp_upper_limit=None, up_clamp_lower_limit=None, gate_up_w_layout=LY.H_X4_INNERMOST,
+                mode=CM.PREFILL, fp8_max=448.0, fp8_round_trip_dtype=nl.float8_e4m3fn,
+            )
+            raise RuntimeError("the up-projection was not captured")
+        except _UpCaptured as c:
+            up = c.up
+        out.update({f"{tag}|codes": codes.view(torch.uint8).numpy(), f"{tag}|rs": rs.numpy(),
+                    f"{tag}|wc": wc.view(torch.uint8).numpy(), f"{tag}|cs": cs.numpy(), f"{tag}|bias": _bf16(bias),
+                    f"{tag}|up": up.float().numpy()})
+    np.savez_compressed(OUT / "qkv_row_mx.npz", **out)
+
+
 def gen_checkpoint():
     comfy = _load_file("ref_comfy_fp8", REF / "diffusion/quantization/comfy_fp8_checkpoint.py")
     m = comfy.build_fp8_dequant_mappings(2)
@@ -319,6 +403,7 @@ def main():
     gen_oproj()
     gen_mlp()
     gen_mlp_row_mx()
+    gen_qkv_row_mx()
     gen_checkpoint()
     for p in sorted(OUT.glob("*.npz")):
         print(p.name, p.stat().st_size)

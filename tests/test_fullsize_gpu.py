@@ -128,3 +128,61 @@ def test_c3_row_scale_linearity(pkg, dev):
     ref = (x[r0:r0 + 64].float() @ w[c0:c0 + 64].float().T) * rs[r0:r0 + 64, None] * cs[None, c0:c0 + 64]
     got = y1[r0:r0 + 64, c0:c0 + 64].float()
     assert float(((got - ref).abs() / ref.abs().clamp(min=1.0)).max()) <= 2 ** -7
+
+
+def test_c4_cp8_shard_pass_plan_vs_exact(pkg, dev):
+    """BASELINE config 4 (S=75600) at CP=8, emulated on one GPU: rank 3's 9450-token query shard
+    against its own block and the 7 remote blocks in the ring's gather order, through the ring's pass
+    plan (local block, then 1, 2, 4 blocks; fp32 partials in between, later passes overlapped). A
+    sample of query rows (3 heads, 48 rows spread over the shard) against the exact CPU attention
+    over all 75600 keys, and the whole shard against one pass over the same keys."""
+    from importlib import import_module
+
+    lib = import_module("vllm-omni-neuron_b200._lib")
+    ring = import_module("vllm-omni-neuron_b200.ring")
+    L = lib.load()
+    S4, world, rank = 75600, 8, 3
+    s = S4 // world
+    g = torch.Generator(device=dev).manual_seed(9)
+    mk = lambda: (torch.randn(1, S4, H, D, generator=g, device=dev) * 0.5).to(torch.bfloat16)  # noqa: E731
+    q, k, v = mk(), mk(), mk()
+    ql = q[:, rank * s:(rank + 1) * s].contiguous()
+    kl, vl = k[:, rank * s:(rank + 1) * s].contiguous(), v[:, rank * s:(rank + 1) * s].contiguous()
+    st = torch.cuda.current_stream().cuda_stream
+    qn2 = torch.empty(H, s, device=dev)
+    km = torch.empty(H, device=dev)
+    qn2_all = torch.empty(H, S4, device=dev)
+    lib.check(L.vomni_cm_prologue(ql.data_ptr(), ql.data_ptr(), 1, s, H, D, qn2.data_ptr(), km.data_ptr(), st), "p")
+    lib.check(L.vomni_cm_prologue(k.data_ptr(), k.data_ptr(), 1, S4, H, D, qn2_all.data_ptr(), km.data_ptr(), st), "p")
+    scale = 1 / math.sqrt(D)
+    order = [ring.source_rank(rank, world, j) for j in range(1, world)]
+    kg = torch.cat([k[:, r * s:(r + 1) * s] for r in order], dim=1).contiguous()
+    vg = torch.cat([v[:, r * s:(r + 1) * s] for r in order], dim=1).contiguous()
+    acc_o = torch.empty(H, s, D, device=dev)
+    acc_l = torch.empty(H, s, device=dev)
+    out = torch.empty(1, H, s, D, dtype=torch.bfloat16, device=dev)
+    lib.check(L.vomni_cm_attend(ql.data_ptr(), kl.data_ptr(), vl.data_ptr(), 1, s, s, 0, s, H, D, scale, qn2.data_ptr(),
+                                km.data_ptr(), acc_o.data_ptr(), acc_l.data_ptr(), 0, None, None, st), "pass0")
+    plan = ring.phase_plan(world)
+    assert plan == [(-1, 1), (0, 1), (1, 2), (3, 4)]
+    for i, (first, count) in enumerate(plan[1:], start=1):
+        fl = lib.CM_ACC_IN | lib.CM_OVERLAP | (lib.CM_FINAL if i == len(plan) - 1 else 0)
+        lib.check(L.vomni_cm_attend(ql.data_ptr(), kg.data_ptr(), vg.data_ptr(), 1, s, (world - 1) * s, first * s,
+                                    count * s, H, D, scale, qn2.data_ptr(), km.data_ptr(), acc_o.data_ptr(),
+                                    acc_l.data_ptr(), fl, out.data_ptr(), None, st), "pass")
+    single = torch.empty(1, H, s, D, dtype=torch.bfloat16, device=dev)
+    lib.check(L.vomni_cm_attend(ql.data_ptr(), k.data_ptr(), v.data_ptr(), 1, s, S4, 0, S4, H, D, scale, qn2.data_ptr(),
+                                km.data_ptr(), None, None, lib.CM_FINAL, single.data_ptr(), None, st), "single")
+    torch.cuda.synchronize()
+    assert lib.device_status() == 0
+    a, b = out.float(), single.float()
+    cos = float((a * b).sum() / torch.sqrt((a * a).sum() * (b * b).sum()))
+    assert cos >= 0.99999 and float((a - b).abs().max()) <= 8e-3, (cos, float((a - b).abs().max()))
+    heads, rows = [0, 21, 39], np.r_[0:16, 4720:4736, s - 16:s]
+    qs = ql[0, rows][:, heads].float().cpu().numpy().transpose(1, 0, 2)[None]  # [1, h, r, d]
+    ks = k[0][:, heads].float().cpu().numpy().transpose(1, 0, 2)[None]
+    vs = v[0][:, heads].float().cpu().numpy().transpose(1, 0, 2)[None]
+    ref = oat.torch_attend(qs, ks, vs, scale)[0]  # [h, r, d]
+    got = out[0][heads][:, rows].float().cpu().numpy()
+    cos = (got * ref).sum() / math.sqrt((got * got).sum() * (ref * ref).sum())
+    assert cos >= 0.9999 and np.abs(got - ref).max() <= 2e-2, (cos, np.abs(got - ref).max())

@@ -213,3 +213,35 @@ def test_mlp_row_mx_oracle_vs_reference_golden(golden):
     assert np.array_equal(codes, g["mxq|codes"])
     ref_deq = (g["mxq|codes"].astype(np.float64) * g["mxq|scale"]).astype(np.float32)
     assert np.array_equal(deq, ref_deq)
+
+
+def test_qkv_row_mx_oracle_vs_reference_golden(golden):
+    """The ROW_MX QKV restatement against the reference's own ROW_MX dequant-matmul, executed from its
+    source: ``_mlp_ref_standard``'s up-projection ``(Xq * row_scale) @ (Wq * w_scale) + bias``
+    (mlp_torch.py:470-497, 575-578; fixture ``make_golden.py qkv_row_mx``) on per-tensor Q/K/V scaled
+    e4m3 weights. The oracle scales after the matmul, as the kernel (``_dequant_row_mx``,
+    qkv_cte.py:3996-4021) does; the two orders differ only by fp32 reassociation, so the fp32 values
+    agree to 2^-20 of the row's magnitude and the bf16 stores are equal except where that noise straddles a
+    bf16 rounding boundary (at most 0.1 % of the elements, apart by at most the noise plus one bf16
+    step)."""
+    from oracle import qkv as oq
+
+    g = golden("qkv_row_mx.npz")
+    for tag in ("a", "b"):
+        codes = g[f"{tag}|codes"]
+        T, H = codes.shape
+        packed = np.concatenate([codes, g[f"{tag}|rs"].astype(np.float32).reshape(-1, 1).view(np.uint8)], axis=1)
+        wc = e4m3fn_from_bits(g[f"{tag}|wc"])  # [H, I]
+        cs, bias, up = g[f"{tag}|cs"], g[f"{tag}|bias"], g[f"{tag}|up"]
+        # the oracle's fp32 pre-store values
+        xc, rs = oq.unpack_row(packed)
+        acc = (xc @ wc) * rs[:, None] * cs[None, :] + bias[None, :]
+        scale = np.abs(up).max(axis=1, keepdims=True)
+        assert (np.abs(acc - up) <= scale * 2.0 ** -20).all(), tag
+        y = oq.row_mx_qkv_ref(packed, wc, cs, bias)
+        ref = bf16_round(up)
+        diff = y != ref
+        assert diff.mean() <= 1e-3, (tag, diff.mean())
+        # one bf16 step is at most |x| * 2^-7; the fp32 noise is bounded per row
+        tol = np.abs(ref) * 2.0 ** -7 + np.broadcast_to(scale, ref.shape) * 2.0 ** -20
+        assert (np.abs(y[diff] - ref[diff]) <= tol[diff]).all(), tag

@@ -194,3 +194,47 @@ def test_mx32_norm_rope_epilogue(pkg, dev):
                           num_kv_heads=heads, cos=cos_rh.reshape(T, 128).cpu().numpy(),
                           sin=sin_rh.reshape(T, 128).cpu().numpy(), eps=1e-6)
     _cmp(y.float().cpu().numpy(), ref, 0.99999, 3e-2, "mx32 epilogue")
+
+
+def test_c3_width_row_and_mx32_vs_oracle(pkg, dev):
+    """BASELINE config 3's projection width, H=5120 -> I=3*5120 (40 heads per segment), on a 512-row
+    slice: the ROW GEMM with the across-heads norm + rotate-half RoPE epilogue against the oracle
+    (pinned to the reference's ROW_MX dequant-matmul by ``qkv_row_mx.npz``), and the MX-32
+    block-scaled GEMM against the oracle on the same dequantised operands. LayerNorm eps 1e-6 and
+    shift/scale ~ N(0, 0.1) as in config 3."""
+    T, H, heads = 512, 5120, 40
+    hidden, w, bias, I = _setup(T, H, heads, dev, seed=7)
+    g = torch.Generator().manual_seed(8)
+    mods = (torch.randn(6, H, generator=g) * 0.1).to(dev)
+    mul, add = (1 + mods[1]).to(torch.bfloat16), mods[0].to(torch.bfloat16)
+    rope = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200.rope")
+    cos, sin = rope.wan_rotary_freqs(128, (1, 2, 2), 1024, (21, 60, 104), device=dev)
+    cos_rh, sin_rh = rope.rope_rotate_half_caches(cos[:, :T], sin[:, :T])
+    kw = dict(num_heads=heads, head_dim=128, num_kv_heads=heads)
+    # ROW
+    packed = pkg.adaln_modulate(hidden, mul, add, eps=1e-6, norm_type="layer_norm", quant="row")
+    wq, chan = pkg.quantize_qkv_weight(w, heads * 128, heads * 128)
+    y = pkg.row_mx_qkv_proj(packed, wq, chan, bias, fused_rope=True, cos_cache=cos_rh, sin_cache=sin_rh,
+                            qk_norm_pre_rope=True, **kw)
+    y_plain = pkg.row_mx_qkv_proj(packed, wq, chan, bias, **kw)
+    torch.cuda.synchronize()
+    pk = packed.view(torch.uint8).cpu().numpy()
+    wc = e4m3fn_from_bits(wq.view(torch.uint8).cpu().numpy()).T  # [H, I]
+    ref_plain = oq.row_mx_qkv_ref(pk, wc, chan.cpu().numpy(), bias.float().cpu().numpy())
+    got = y_plain.float().cpu().numpy()
+    _cmp(got, ref_plain, 0.99999, 1e-2 * max(1.0, np.abs(ref_plain).max()), "C3 ROW gemm")
+    assert (np.abs(got - ref_plain) <= np.abs(ref_plain) * 2 ** -7 + 1e-3).mean() > 0.999
+    ref = oq.qkv_epilogue(ref_plain, gamma_q=None, gamma_k=None, cos=cos_rh.reshape(T, 128).cpu().numpy(),
+                          sin=sin_rh.reshape(T, 128).cpu().numpy(), eps=1e-6, **kw)
+    _cmp(y.float().cpu().numpy(), ref, 0.99999, 3e-2, "C3 ROW gemm + norm + RoPE")
+    # MX-32
+    xc, xs = pkg.adaln_modulate(hidden, mul, add, eps=1e-6, norm_type="layer_norm", quant="mx32")
+    wmc, wms, wmsp = pkg.quantize_qkv_weight_mx32(w)
+    ym = pkg.mx32_qkv_proj((xc, xs), wmc, wmsp, bias, **kw)
+    torch.cuda.synchronize()
+    deq = lambda c, s: (e4m3fn_from_bits(c.view(torch.uint8).cpu().numpy()).reshape(c.shape[0], -1, 32)
+                        * np.exp2(s.cpu().numpy().astype(np.float64) - 127)[..., None]).reshape(c.shape[0], -1)
+    ref_mx = oq.mx32_qkv_ref(deq(xc, xs), deq(wmc, wms).T, bias.float().cpu().numpy())
+    got_mx = ym.float().cpu().numpy()
+    _cmp(got_mx, ref_mx, 0.99999, 1e-2 * max(1.0, np.abs(ref_mx).max()), "C3 MX-32 gemm")
+    assert (np.abs(got_mx - ref_mx) <= np.abs(ref_mx) * 2 ** -7 + 1e-3).mean() > 0.999
