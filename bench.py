@@ -586,6 +586,19 @@ def run_oproj(args, emit):
         y = pkg.wan_o_proj(active, w, bias)
         return pkg.adaln_modulate(y, n2w, n2b, eps=1e-6, quant="row", residual=res, gate=gate)
 
+    # FP8 (ROW) o-projection: per-token row quant of the d-major activation + FP8 ROW GEMM
+    w8, w8_scale = pkg.quantize_qkv_weight(w.float(), H, 0)
+    codes8 = torch.empty(S, K, dtype=torch.float8_e4m3fn, device=dev)
+    scales8 = torch.empty(S, dtype=torch.float32, device=dev)
+    L = lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def fp8():
+        return pkg.row_mx_o_proj(active, w8, w8_scale, bias)
+
+    def fp8_quant():
+        lib.check(L.vomni_oproj_rowquant(active.data_ptr(), 1, K, S, codes8.data_ptr(), scales8.data_ptr(), st), "rowquant")
+
     def timeit(fn, n):
         ts = []
         for _ in range(n):
@@ -598,7 +611,7 @@ def run_oproj(args, emit):
             ts.append(a.elapsed_time(b))
         return statistics.median(ts)
 
-    for fn in (proj, fused, fused_norm2, unfused_norm2):
+    for fn in (proj, fused, fused_norm2, unfused_norm2, fp8, fp8_quant):
         for _ in range(args.warmup):
             fn()
     torch.cuda.synchronize()
@@ -606,6 +619,7 @@ def run_oproj(args, emit):
     sampler = ClockSampler(0)
     sampler.start()
     t_p, t_f, t_fn, t_un = timeit(proj, n), timeit(fused, n), timeit(fused_norm2, n), timeit(unfused_norm2, n)
+    t_8, t_8q = timeit(fp8, n), timeit(fp8_quant, n)
     clocks = sampler.stop()
     assert lib.device_status() == 0
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
@@ -622,9 +636,15 @@ def run_oproj(args, emit):
             "oproj_gemm_gated_residual": {"ms": round(t_f, 4), "TFLOP/s": round(flops / t_f / 1e9, 1)},
             "fused_step": {"ms": round(t_fn, 4), "kernels": "gemm_bf16_pair_kernel<0,1> (residual epilogue) + adaln_kernel"},
             "unfused_step": {"ms": round(t_un, 4), "kernels": "gemm_bf16_pair_kernel<0,0> + adaln_kernel (residual step)"},
+            "row_mx_o_proj_fp8": {"ms": round(t_8, 4), "TFLOP/s": round(flops / t_8 / 1e9, 1),
+                                  "frac_of_2x_measured_bf16_burst": round(flops / t_8 / 1e9 / (2 * bf16), 4),
+                                  "kernels": "oproj_rowquant_kernel + qkv_gemm_pair_kernel<0>"},
+            "oproj_rowquant": {"ms": round(t_8q, 4), "bytes": S * K * 2 + S * K + S * 4,
+                               "GB/s": round((S * K * 3 + S * 4) / t_8q / 1e6, 1),
+                               "frac_of_measured_hbm": round((S * K * 3 + S * 4) / t_8q / 1e6 / peaks.get("hbm_gbs", 6650.0), 4)},
         },
         "clocks": clocks,
-        "gpu_launches": 5 * n,
+        "gpu_launches": 8 * n,
     })
 
 

@@ -91,3 +91,77 @@ def test_errors(pkg, dev):
     lib = pytest.importorskip("importlib").import_module("vllm-omni-neuron_b200._lib")
     with pytest.raises(lib.VomniError):
         pkg.wan_o_proj(a, torch.zeros(256, 200, dtype=torch.bfloat16, device=dev), None)  # H % 32
+
+
+def _fp8_oproj_case(pkg, dev, B, N, S, H, seed):
+    g = torch.Generator().manual_seed(seed)
+    K = N * 128
+    active = (torch.randn(B, N, 128, S, generator=g) * 0.5).to(torch.bfloat16)
+    active[:, :, :, ::7] *= 30  # tokens with larger magnitudes: per-token scales differ
+    w = torch.randn(K, H, generator=g) * 0.02
+    bias = (torch.randn(H, generator=g) * 0.1).to(torch.bfloat16)
+    codes, chan = pkg.quantize_qkv_weight(w.to(dev), H, 0)  # [H, K] e4m3, one per-tensor scale
+    return active, codes, chan, bias
+
+
+@pytest.mark.parametrize("B,N,S,H", [(1, 4, 1000, 512), (2, 2, 136, 768), (1, 1, 9, 256)])
+def test_row_mx_o_proj_vs_oracle(pkg, dev, B, N, S, H):
+    """FP8 o-projection (row_mx_kernels.py:114-138): the per-token ROW codes and scales of the d-major
+    activation bit-exact against the oracle's ROW quantiser, and the projection against the oracle
+    on the same codes (identical FP8 operands: fp32 accumulation order and the bf16 store differ)."""
+    from importlib import import_module
+
+    from oracle.numerics import e4m3fn_from_bits
+
+    lib = import_module("vllm-omni-neuron_b200._lib")
+    active, codes, chan, bias = _fp8_oproj_case(pkg, dev, B, N, S, H, seed=40 + S)
+    y = pkg.row_mx_o_proj(active.to(dev), codes, chan.reshape(1, -1).expand(128, -1), bias.reshape(1, -1).to(dev))
+    # the quantiser alone, on the 8-padded token count
+    s_pad = -(-S // 8) * 8
+    act = torch.nn.functional.pad(active, (0, s_pad - S)).to(dev).contiguous()
+    qc = torch.empty(B * s_pad, N * 128, dtype=torch.float8_e4m3fn, device=dev)
+    qs = torch.empty(B * s_pad, dtype=torch.float32, device=dev)
+    lib.check(lib.load().vomni_oproj_rowquant(act.data_ptr(), B, N * 128, s_pad, qc.data_ptr(), qs.data_ptr(),
+                                              torch.cuda.current_stream().cuda_stream), "rowquant")
+    torch.cuda.synchronize()
+    assert tuple(y.shape) == (B, S, H)
+    wc = e4m3fn_from_bits(codes.view(torch.uint8).cpu().numpy())  # [H, K]
+    ref, (ref_codes, ref_scale) = oop.row_mx_o_proj_ref(active.float().numpy(), wc, chan.cpu().numpy(),
+                                                        bias.float().numpy())
+    got_codes = e4m3fn_from_bits(qc.view(torch.uint8).cpu().numpy()).reshape(B, s_pad, -1)[:, :S].reshape(B * S, -1)
+    got_scale = qs.cpu().numpy().reshape(B, s_pad)[:, :S].reshape(-1)
+    assert np.array_equal(got_scale, ref_scale)
+    assert np.array_equal(got_codes, ref_codes)
+    got = y.float().cpu().numpy()
+    cos = (got * ref).sum() / np.sqrt((got * got).sum() * (ref * ref).sum())
+    assert cos >= 0.99999 and np.abs(got - ref).max() <= 1e-2 * max(1.0, np.abs(ref).max())
+    assert (np.abs(got - ref) <= np.abs(ref) * 2 ** -7 + 1e-3).mean() > 0.999
+    assert lib.device_status() == 0
+
+
+def test_row_mx_o_proj_layouts_and_leaf(pkg, dev):
+    """The reference's [N*D//4, H, 4] weight pack gives the same result as [H, N*D] codes, and the
+    FP8 self-attention leaf with o-projection weights returns row_mx_o_proj of its attention."""
+    B, N, S, H = 1, 2, 256, 512
+    active, codes, chan, bias = _fp8_oproj_case(pkg, dev, B, N, S, H, seed=3)
+    K = N * 128
+    w3 = codes.view(torch.uint8).t().reshape(K // 4, 4, H).permute(0, 2, 1).contiguous().view(torch.float8_e4m3fn)
+    a = pkg.row_mx_o_proj(active.to(dev), codes, chan, bias.to(dev))
+    b = pkg.row_mx_o_proj(active.to(dev), w3, chan.reshape(1, -1).expand(128, -1), bias.reshape(1, -1).to(dev))
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    # leaf: FP8 QKV -> attention -> FP8 o-projection
+    g = torch.Generator().manual_seed(4)
+    Hid = 256
+    hidden = torch.randn(B, S, Hid, generator=g).to(torch.bfloat16).to(dev)
+    wqkv = (torch.randn(Hid, 3 * K, generator=g) * 0.02).to(dev)
+    wq, qchan = pkg.quantize_qkv_weight(wqkv, K, K)
+    packed = pkg.adaln_modulate(hidden, None, None, eps=1e-6, norm_type="layer_norm", quant="row")
+    attn = pkg.wan_self_attention_fp8(packed, wq, qchan, None, None, None, num_heads=N)
+    wo = torch.randn(K, Hid, generator=g) * 0.02
+    oc, ochan = pkg.quantize_qkv_weight(wo.to(dev), Hid, 0)
+    out = pkg.wan_self_attention_fp8(packed, wq, qchan, None, None, None, num_heads=N, o_proj_weight=oc,
+                                     o_proj_w_scale=ochan, o_proj_bias=None)
+    torch.cuda.synchronize()
+    assert tuple(out.shape) == (B, S, Hid)
+    assert torch.equal(out, pkg.row_mx_o_proj(attn, oc, ochan, None))

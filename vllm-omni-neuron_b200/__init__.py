@@ -7,7 +7,7 @@ Drop-in for the vllm-omni-neuron plugin's attention processor and kernel-call AP
 * :func:`adaln_modulate` — fused gated-residual + (Layer|RMS)Norm + modulation + FP8 row quant
 * :func:`row_mx_qkv_proj` — FP8 QKV projection with across-heads RMS norm + rotate-half RoPE
 * :func:`wan_o_proj`, :func:`attn_out_norm2` — output projection of the d-major attention output,
-  with the block's gated residual + norm2 adaLN
+  with the block's gated residual + norm2 adaLN; :func:`row_mx_o_proj` — its FP8 (ROW) form
 * :func:`wan_mlp` — the block's FFN (GELU-tanh MLP); :func:`row_mx_mlp` — its FP8 (ROW_MX) leaf
 * :func:`wan_block_forward` — a whole transformer block (self-attn + cross-attn + FFN, bf16 leaves)
 * :func:`cfg_gather_combine` — the CFG-parallel gather + combine of the two branch outputs
@@ -25,7 +25,7 @@ from .cfg import cfg_combine, cfg_gather_combine
 from .dit import cp_gather_sequence, cp_shard_sequence, wan_blocks_forward, wan_output_head
 from .ffn import quantize_mlp_weights_row_mx, row_mx_mlp, wan_mlp
 from .leaf import project_cross_kv_fp8, wan_cross_attention_fp8, wan_self_attention_fp8
-from .oproj import attn_out_norm2, o_proj_gated_residual, wan_o_proj
+from .oproj import attn_out_norm2, o_proj_gated_residual, row_mx_o_proj, wan_o_proj
 from .qkv import (
     mx32_qkv_proj,
     pack_mx_scales,
@@ -60,6 +60,7 @@ __all__ = [
     "repack_mx_contiguous",
     "ring_attention_const_max_fwd",
     "row_mx_mlp",
+    "row_mx_o_proj",
     "row_mx_qkv_proj",
     "wan_block_forward",
     "wan_blocks_forward",

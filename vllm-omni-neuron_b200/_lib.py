@@ -43,6 +43,7 @@ SIGNATURES = {
     "vomni_qkv_fp8_gemm": (c_int, [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P]),
     "vomni_qk_norm_rope": (c_int, [P, c_int, c_int, c_int, c_int, c_int, P, c_float, P, P, P, P, P]),
     "vomni_oproj_gemm": (c_int, [P, c_int, c_int, c_int, P, P, c_int, P, P, c_int, P, P]),
+    "vomni_oproj_rowquant": (c_int, [P, c_int, c_int, c_int, P, P, P]),
     "vomni_cfg_combine": (c_int, [P, P, P, ctypes.c_longlong, c_int, ctypes.c_float, P]),
     "vomni_ffn_fp8_up": (c_int, [P, P, P, P, P, c_int, c_int, c_int, P, P, P]),
     "vomni_ffn_fp8_down": (c_int, [P, P, P, P, P, P, c_int, c_int, c_int, P, P, ctypes.c_longlong, P, P]),

@@ -278,6 +278,88 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------- FP8 (ROW) o-projection input
+// row_mx_o_proj (diffusion/quantization/row_mx_kernels.py:114-138) quantises the d-major attention
+// output inside its NKI kernel, one scale per token over the token's N*D values (ROW), then runs the
+// FP8 GEMM. This kernel does the quantisation with the ROW rule of the in-tree NKI ROW quantiser
+// (scale = max(amax / 448, 1e-6), codes = e4m3fn(x * (1 / scale)), adaln_quant.py:520-536) and
+// writes token rows, so the FP8 ROW GEMM of the QKV projection consumes them unchanged. A CTA takes
+// kTok tokens of one batch element: 16-byte loads along the tokens of each of the K rows into shared
+// memory (stored token-major, rows padded so the later column reads hit distinct banks), a |max|
+// per token over K, then 16-byte code stores along K. The d-major input is read once.
+constexpr int kQuantTok = 8;
+constexpr int kQuantThreads = 256;
+constexpr int kQuantPad = 8;  // bf16 elements of row padding: 16-byte aligned rows, 4-bank row offset
+constexpr int kQuantUnroll = 8;
+__global__ void __launch_bounds__(kQuantThreads) oproj_rowquant_kernel(const __nv_bfloat16* __restrict__ attn, int K, int S,
+                                                                      uint8_t* __restrict__ codes,
+                                                                      float* __restrict__ scales) {
+  extern __shared__ __align__(16) uint8_t smem_q[];
+  const int ld = K + kQuantPad;
+  __nv_bfloat16* sx = reinterpret_cast<__nv_bfloat16*>(smem_q);                  // [kTok][K + pad]
+  float* red = reinterpret_cast<float*>(smem_q + static_cast<size_t>(kQuantTok) * ld * 2);  // [slices][kTok]
+  float* sinv = red + kQuantThreads;                                              // [kTok]
+  const int b = blockIdx.y;
+  const int tok0 = blockIdx.x * kQuantTok;
+  const __nv_bfloat16* src = attn + static_cast<size_t>(b) * K * S + tok0;
+  const bool full = tok0 + kQuantTok <= S;  // S % 8 == 0: a block is either whole or empty past S
+  if (full) {
+    // kQuantUnroll independent 16-byte loads in flight per thread before their shared-memory stores
+    for (int k0 = threadIdx.x; k0 < K; k0 += kQuantThreads * kQuantUnroll) {
+      uint4 v[kQuantUnroll];
+#pragma unroll
+      for (int u = 0; u < kQuantUnroll; ++u) {
+        const int k = k0 + u * kQuantThreads;
+        v[u] = k < K ? __ldcs(reinterpret_cast<const uint4*>(src + static_cast<size_t>(k) * S)) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kQuantUnroll; ++u) {
+        const int k = k0 + u * kQuantThreads;
+        if (k >= K) break;
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[u]);
+#pragma unroll
+        for (int t = 0; t < kQuantTok; ++t) sx[t * ld + k] = e[t];
+      }
+    }
+  }
+  __syncthreads();
+  if (!full) return;
+  // |max| per token: thread (t, slice) scans every slices-th k of token t
+  constexpr int kSlices = kQuantThreads / kQuantTok;
+  const int tt = threadIdx.x % kQuantTok, sl = threadIdx.x / kQuantTok;
+  float m = 0.f;
+  for (int k = sl; k < K; k += kSlices) m = fmaxf(m, fabsf(__bfloat162float(sx[tt * ld + k])));
+  red[sl * kQuantTok + tt] = m;
+  __syncthreads();
+  if (threadIdx.x < kQuantTok) {
+    float a = 0.f;
+    for (int i = 0; i < kSlices; ++i) a = fmaxf(a, red[i * kQuantTok + threadIdx.x]);
+    const float scale = fmaxf(a / 448.f, 1e-6f);
+    sinv[threadIdx.x] = __frcp_rn(scale);
+    scales[static_cast<size_t>(b) * S + tok0 + threadIdx.x] = scale;
+  }
+  __syncthreads();
+  // codes: consecutive threads take consecutive 16-value chunks of one token row
+  const int nchunk = K / 16;
+  for (int i = threadIdx.x; i < kQuantTok * nchunk; i += kQuantThreads) {
+    const int t = i / nchunk, c = i - t * nchunk;
+    const float inv = sinv[t];
+    const uint4* row = reinterpret_cast<const uint4*>(sx + t * ld + c * 16);
+    const uint4 h0 = row[0], h1 = row[1];
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&h0);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&h1);
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162* q = j < 2 ? a2 + 2 * j : b2 + 2 * (j - 2);
+      const float2 f0 = __bfloat1622float2(q[0]), f1 = __bfloat1622float2(q[1]);
+      w[j] = e4m3x2(f0.x * inv, f0.y * inv) | (static_cast<uint32_t>(e4m3x2(f1.x * inv, f1.y * inv)) << 16);
+    }
+    __stcs(reinterpret_cast<uint4*>(codes + (static_cast<size_t>(b) * S + tok0 + t) * K) + c, make_uint4(w[0], w[1], w[2], w[3]));
+  }
+}
+
 int ensure_smem_attr() {
   // once per kernel and device (ensure_max_smem caches)
   int rc = 0;
@@ -337,6 +419,24 @@ extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const voi
   auto kern = residual ? oproj::gemm_bf16_pair_kernel<false, oproj::EPI_RESIDUAL>
                        : oproj::gemm_bf16_pair_kernel<false, oproj::EPI_BIAS>;
   kern<<<2 * pairs, oproj::kThreads, oproj::kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  VOMNI_CUDA_TRY(cudaGetLastError());
+  return VOMNI_OK;
+}
+
+extern "C" int vomni_oproj_rowquant(const void* attn, int b, int k, int s, void* codes, float* scales,
+                                    vomni_stream_t stream) {
+  if (!attn || !codes || !scales) return VOMNI_EINVAL;
+  if (b <= 0 || k <= 0 || s <= 0 || (k % 16) || (s % 8) || b > 65535) return VOMNI_EBADSHAPE;
+  const size_t smem = static_cast<size_t>(oproj::kQuantTok) * (k + oproj::kQuantPad) * 2 + (oproj::kQuantThreads + oproj::kQuantTok) * 4;
+  if (smem > 227 * 1024) return VOMNI_EBADSHAPE;
+  if ((reinterpret_cast<uintptr_t>(attn) | reinterpret_cast<uintptr_t>(codes)) & 15) return VOMNI_EALIGN;
+  int rc = require_sm100();
+  if (rc) return rc;
+  rc = ensure_max_smem(oproj::oproj_rowquant_kernel, static_cast<int>(smem));
+  if (rc) return rc;
+  const dim3 grid((s + oproj::kQuantTok - 1) / oproj::kQuantTok, b);
+  oproj::oproj_rowquant_kernel<<<grid, oproj::kQuantThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(attn), k, s, static_cast<uint8_t*>(codes), scales);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }

@@ -8,6 +8,10 @@
   with the gated residual ``hidden_states + gate_msa * attn1_out`` fused into its epilogue, then
   the norm2 adaLN (affine LayerNorm, or none) with the quantisation the next leaf wants. Returns
   ``(hidden_states, norm_h)`` as the reference's ``adaln_modulate(..., residual=, gate=)`` does.
+* :func:`row_mx_o_proj` keeps the reference's FP8 o-projection ``row_mx_o_proj(attention, weight,
+  weight_scales, bias)`` (vllm_omni_neuron/diffusion/quantization/row_mx_kernels.py:114-138): the
+  d-major bf16 attention is ROW-quantised per token (``vomni_oproj_rowquant``) and projected by the
+  FP8 ROW GEMM (``vomni_qkv_fp8_gemm``): ``y = bf16((Xq @ Wq^T) * row_scale * w_scale + bias)``.
 """
 
 from __future__ import annotations
@@ -101,3 +105,48 @@ def attn_out_norm2(
     t = o_proj_gated_residual(attention, o_proj_weight, o_proj_bias, hidden_states, gate_msa)
     norm_h = adaln_modulate(t, norm2_weight, norm2_bias, eps=eps, norm_type=norm_type, quant=quant)
     return t, norm_h
+
+
+def row_mx_o_proj(attention: torch.Tensor, weight: torch.Tensor, weight_scales: torch.Tensor,
+                  bias: torch.Tensor | None) -> torch.Tensor:
+    """FP8 o-projection of the d-major ``[B, N, D, S]`` bf16 attention -> ``[B, S, H]`` bf16.
+
+    ``weight``: the reference's ``[N*D//4, H, 4]`` FP8 pack (row_mx_modules.py:243-250) or this
+    build's ``[H, N*D]`` K-major codes (``quantize_qkv_weight(w, H, 0)``). ``weight_scales``: the
+    per-channel weight scale, ``[128, H]`` (the reference's expanded scalar), ``[1, H]`` or ``[H]``.
+    The reference's kernel (nkilib ``output_projection_cte``) is not in its source tree, so the
+    activation quantisation follows its in-tree ROW rule (adaln_quant.py:520-536)."""
+    from .qkv import repack_mx_contiguous
+
+    if attention.dim() != 4 or attention.dtype != torch.bfloat16:
+        raise ValueError(f"attention must be d-major bf16 [B, N, D, S], got {tuple(attention.shape)} {attention.dtype}")
+    if not attention.is_cuda:
+        raise RuntimeError("attention must be a CUDA tensor (the B200 kernel has no CPU path)")
+    B, N, D, S = attention.shape
+    K = N * D
+    if weight.dim() == 3:
+        weight = repack_mx_contiguous(weight)
+    H = weight.shape[0]
+    if weight.shape[1] != K:
+        raise ValueError(f"weight contraction {weight.shape[1]} != N*D = {K}")
+    chan = weight_scales.reshape(-1, H)[0].float().contiguous()
+    b = bias.reshape(-1).to(torch.bfloat16).contiguous() if bias is not None else None
+    s_pad = -(-S // 8) * 8
+    act = attention.contiguous()
+    if s_pad != S:
+        act = torch.nn.functional.pad(act, (0, s_pad - S))
+    dev = act.device
+    T = B * s_pad
+    codes = torch.empty(T, K, dtype=torch.float8_e4m3fn, device=dev)
+    scales = torch.empty(T, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    L = _lib.load()
+    _lib.check(L.vomni_oproj_rowquant(act.data_ptr(), B, K, s_pad, codes.data_ptr(), scales.data_ptr(), st),
+               "vomni_oproj_rowquant")
+    y = torch.empty(B, s_pad, H, dtype=torch.bfloat16, device=dev)
+    _lib.check(
+        L.vomni_qkv_fp8_gemm(codes.data_ptr(), scales.data_ptr(), weight.contiguous().data_ptr(), chan.data_ptr(),
+                             b.data_ptr() if b is not None else None, T, K, H, H, 0, y.data_ptr(), None, st),
+        "vomni_qkv_fp8_gemm",
+    )
+    return y if s_pad == S else y[:, :S].contiguous()
