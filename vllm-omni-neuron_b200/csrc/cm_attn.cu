@@ -10,14 +10,15 @@
 //
 // Kernel layout: a cluster of two CTAs on two SMs (tcgen05 cta_group::2) covers 2 x 256 query rows
 // of one (batch, head); query tile t of the pair is 256 rows, 128 in each CTA. Per CTA:
-//   warp 0      TMA producer: its halves of both Q tiles once, then K/V 128-key tiles into 2-stage
-//               rings (no multicast)
+//   warp 0      TMA producer: its halves of both Q tiles once, then K/V 128-key tiles into rings
+//               (no multicast)
 //   warp 1      TMEM owner; in the even CTA also the MMA issuer (one elected lane):
 //               S_t = Q_t K^T (SS form), O_t += P_t V (TS form, P read straight from TMEM)
-//   warps 2..5  softmax of query tile 0, warps 6..9 of query tile 1: one query row per thread (TMEM
-//               lane), P = exp2(S*scale*log2e - c*log2e) written back to TMEM as bf16 over S, then
-//               the epilogue (normalise / partial write). The two warpgroups ping-pong: while one
-//               computes exponentials the tensor pipe runs the other tile's PV and next QK.
+//   warps 2..9  softmax + epilogue: both warpgroups work on every tile, warpgroup 0 on keys 0-63 and
+//               warpgroup 1 on keys 64-127 of each step; one query row per thread (TMEM lane),
+//               P = exp2(S*scale*log2e - c*log2e) written back to TMEM as bf16 over S. The tiles
+//               ping-pong: while the softmax warps exponentiate one tile, the tensor pipe runs the
+//               other tile's PV and next QK.
 // TMEM columns: S0/P0 [0,128) S1/P1 [128,256) O0 [256,384) O1 [384,512).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -36,6 +37,11 @@
 #ifndef VOMNI_CM_POLY_PAIRS
 #define VOMNI_CM_POLY_PAIRS 0
 #endif
+// Depth of the K/V shared-memory ring (one stage = the K and V halves of one 128-key step,
+// 32 KB per CTA of a pair). A stage is released one step after its K was consumed (with its V).
+#ifndef VOMNI_CM_KV_STAGES
+#define VOMNI_CM_KV_STAGES 3
+#endif
 
 namespace vomni {
 namespace cm {
@@ -48,9 +54,31 @@ constexpr uint32_t kTileBytes = kTile * kD * 2;  // 32 KB: one bf16 [128 x 128] 
 constexpr uint32_t kHalfBytes = kTileBytes / 2;  // 16 KB: one [128 x 64] swizzled half
 constexpr int kPolyPairs = VOMNI_CM_POLY_PAIRS;
 static_assert(kPolyPairs >= 0 && kPolyPairs <= 8, "VOMNI_CM_POLY_PAIRS is a count out of 8 column pairs");
+constexpr int kKV = VOMNI_CM_KV_STAGES;
+static_assert(kKV >= 2 && kKV <= 5, "K/V ring depth");
 
-// S_FULL: one barrier per query tile t at index 2t. P_FULL: one per (tile t, key half h) at 2t + h.
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9, P_FULL = 13, O_FULL = 17, NBAR = 18 };
+// K/V ring barriers: one FULL and one EMPTY per stage (K and V of a step travel together). S_FULL +
+// 2t: S of tile t complete. P_FULL + 2t + set: the set-th 32-key chunk of both warpgroups' key
+// halves of tile t is in TMEM (one arrival per softmax warp of both CTAs). O_FULL + t: the last PV of
+// tile t is complete.
+enum Bar : int {
+  Q_FULL = 0,
+  KV_FULL = 1,
+  KV_EMPTY = KV_FULL + kKV,
+  S_FULL = KV_EMPTY + kKV,
+  P_FULL = S_FULL + 4,
+  O_FULL = P_FULL + 4,
+  NBAR = O_FULL + kQT
+};
+constexpr uint32_t kPWarps = 16;  // softmax warps of both CTAs: arrivals per P barrier phase
+// P publication granularity: 2 = each tile's P in two chunk sets (the PV MMAs of the first set start
+// while the second is exponentiated), 1 = whole tiles (one MMA-thread wait per tile and step).
+#ifndef VOMNI_CM_P_SETS
+#define VOMNI_CM_P_SETS 2
+#endif
+constexpr int kPSets = VOMNI_CM_P_SETS;
+static_assert(kPSets == 1 || kPSets == 2, "P sets per tile");
+static_assert(NBAR * 8 + 8 <= 256, "barriers, TMEM slot and abort flag fit the 256-byte area");
 
 // TMEM columns: tile t owns S_t = [t*128, t*128+128) (P_t, bf16, aliases its first 64 columns) and
 // O_t = [256 + t*128, 256 + t*128 + 128).
@@ -84,11 +112,11 @@ __host__ __device__ constexpr bool poly_pair(int i) {
 // One 32-column chunk of one query row: p = 2^(s*scale*log2e - c*log2e), packed to bf16 pairs for
 // the PV MMA, and the row sum accumulated from those same bf16 values: the reference sums exactly
 // the bf16 P it multiplies, through the ones column of [V|1] (attention_const_max.py:307-311,
-// 370-379). The scale-and-shift and the sum run as packed fp32 pairs; two independent accumulator
-// pairs keep the add chain short. kMask: columns at or past `valid` (keys outside this pass)
-// contribute 0.
+// 370-379). The scale-and-shift runs as packed fp32 pairs; the sum adds the bf16 values exactly
+// into four independent fp32 accumulators (short add chains). kMask: columns at or past `valid`
+// (keys outside this pass) contribute 0.
 template <bool kMask>
-VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], uint64_t scale2, uint64_t neg_c2, int valid, uint64_t (&acc)[2],
+VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], uint64_t scale2, uint64_t neg_c2, int valid, float (&acc)[4],
                              uint32_t (&pk)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -106,117 +134,143 @@ VOMNI_DEV void softmax_chunk(const uint32_t (&s)[32], uint64_t scale2, uint64_t 
       p1 = (2 * i + 1 < valid) ? p1 : 0.f;
     }
     pk[i] = pack_bf16x2(p0, p1);
-    acc[i & 1] = f2_add(acc[i & 1], f2_pack(__uint_as_float(pk[i] << 16), __uint_as_float(pk[i] & 0xffff0000u)));
+    add_bf16x2_f32(acc[(i & 1) * 2], acc[(i & 1) * 2 + 1], pk[i]);
   }
 }
 
-// Signal that this warp's P columns are in TMEM: one arrival per warp on the pair leader's barrier.
-VOMNI_DEV void publish_p(uint32_t bar_cluster) {
+
+// Signal that this warp's P columns of one (tile, chunk set) are in TMEM, after its stores completed
+// (tcgen05.wait::st + fence::before_thread_sync): one arrival per warp on the set's barrier in the
+// pair leader (release at cluster scope). `pbar`: shared::cluster address of the leader's P barriers.
+VOMNI_DEV void publish_p(uint32_t pbar, int set) {
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(bar_cluster);
+  if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(pbar + 8 * set);
 }
 
-// Whole-tile softmax that publishes P in two halves: keys 0-63 (P columns 0-31) are signalled on
-// `p_lo` as soon as they are in TMEM, so the PV MMAs over them overlap the exponentials of keys
-// 64-127. The S columns 64-127 are loaded while keys 0-63 are computed.
+// P layout in TMEM: the bf16 probabilities of keys [16kk, 16kk + 16) of query tile t sit in the 8
+// columns from S_t + p_col(kk). Warpgroup 0 owns keys 0-63 (S columns 0-63) and writes their P over
+// its first 32 S columns; warpgroup 1 owns keys 64-127 (S columns 64-127) and writes their P over
+// columns 64-95. Neither overwrites S that the other, or its own not yet loaded chunk, still reads.
+__host__ __device__ constexpr uint32_t p_col(int kk) { return kk * 8 + (kk >= 4 ? 32 : 0); }
+
+// Softmax of warpgroup wg's share of one query tile: keys [64wg, 64wg + 64) of this thread's row,
+// in two 32-key chunks published separately: chunk A (keys 64wg .. +32) on p_a, chunk B on p_b
+// (the caller publishes B after its store completes). Chunk B's S is loaded while chunk A is
+// computed; chunk A's P lands on chunk A's own S columns, chunk B's S columns are never written.
 template <bool kMask>
-VOMNI_DEV void softmax_tile_split(uint32_t col_s, uint64_t scale2, uint64_t neg_c2, int valid, uint64_t (&acc)[2],
-                                  uint32_t p_lo_cluster) {
-  uint32_t s0[32], s1[32], s2[32], s3[32];
-  tmem_ld32(col_s, s0);
-  tmem_ld32(col_s + 32, s1);
-  tmem_ld_wait(s0);
-  tmem_ld_wait(s1);
-  tmem_ld32(col_s + 64, s2);
-  tmem_ld32(col_s + 96, s3);
-  uint32_t pk[16];
-  softmax_chunk<kMask>(s0, scale2, neg_c2, valid, acc, pk);
-  tmem_st16(col_s, pk);
-  softmax_chunk<kMask>(s1, scale2, neg_c2, valid - 32, acc, pk);
-  tmem_st16(col_s + 16, pk);
-  tmem_st_wait();
-  tc_fence_before();
-  publish_p(p_lo_cluster);
-  tmem_ld_wait(s2);
-  tmem_ld_wait(s3);
-  softmax_chunk<kMask>(s2, scale2, neg_c2, valid - 64, acc, pk);
-  tmem_st16(col_s + 32, pk);
-  softmax_chunk<kMask>(s3, scale2, neg_c2, valid - 96, acc, pk);
-  tmem_st16(col_s + 48, pk);
-}
-
-// K stage j%2 is free once S of the last query tile for step j is complete; V stage (j-1)%2 too
-// (its PV MMAs were issued before that QK). Replaces two tcgen05.commit per step on the MMA thread.
-VOMNI_DEV void release_stages(uint64_t* bars, int j) {
-  mbar_arrive(&bars[K_EMPTY + (j & 1)]);
-  if (j > 0) mbar_arrive(&bars[V_EMPTY + ((j - 1) & 1)]);
-}
-
-// Softmax + epilogue warpgroups (warps 2..9): query tile t = (warp-2)/4, one query row per thread.
-// q_base: first query row of this CTA's tile 0; tile_stride: rows between its tiles. The P
-// barriers live in the pair leader and take one arrival per warp (p_full_cluster = their
-// shared::cluster address).
-VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort_flag, uint32_t tbase, int warp, int lane,
-                            int q_base, int tile_stride, int bh, int n_tiles, uint32_t p_full_cluster) {
-  const int t = (warp - 2) >> 2;  // query tile of this warpgroup
-  const int quad = warp & 3;      // TMEM lane quadrant this warp may access
-  const int row = quad * 32 + lane;
-  const int grow = q_base + t * tile_stride + row;
-  const bool row_ok = grow < p.s_q;
-  const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-  const uint32_t col_s = tbase + lane_addr + kColS + t * 128;
-  const uint32_t col_o = tbase + lane_addr + kColO + t * 128;
-  const size_t rowidx = static_cast<size_t>(bh) * p.s_q + grow;
-  float c = 0.f;
-  if (row_ok) {
-    // c_i = scale * sqrt(kmax2 * ||q_i||^2), held in bf16 like the reference's c_row
-    // (ring_attention_const_max_fwd.py:585-591).
-    const float c32 = p.scale * sqrtf(p.kmax2[bh] * p.qn2[rowidx]);
-    c = __bfloat162float(__float2bfloat16_rn(c32));
-  }
-  const float neg_c = -c * 1.4426950408889634f;
-  const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
-  const uint64_t neg_c2 = f2_pack(neg_c, neg_c);
-  // One thread of the last tile's warpgroup frees the K/V stages: S_{last}(j) complete means
-  // every QK of step j (and, issued before it, every PV of step j-1) has finished reading them.
-  const bool releaser = (t == kQT - 1) && row == 0;
-  uint64_t acc[2] = {0ull, 0ull};  // two (fp32, fp32) pairs, +0.0f bit patterns
-  bool ok = true;
-  for (int j = 0; j < n_tiles && ok; ++j) {
-    const int valid = p.n_keys - j * kTile;  // keys of this tile inside the pass's range
-    if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
-    tc_fence_after();
-    if (releaser) release_stages(bars, j);
-    if (valid >= kTile)
-      softmax_tile_split<false>(col_s, scale2, neg_c2, valid, acc, p_full_cluster + (2 * t) * 8);
-    else
-      softmax_tile_split<true>(col_s, scale2, neg_c2, valid, acc, p_full_cluster + (2 * t) * 8);
+VOMNI_DEV void softmax_share(uint32_t col_s, int wg, uint64_t scale2, uint64_t neg_c2, int valid, float (&acc)[4],
+                             uint32_t pbar, int set_a) {
+  uint32_t sa[32], sb[32], pk[16];
+  const uint32_t c0 = col_s + 64 * wg;
+  const int v0 = valid - 64 * wg;
+  tmem_ld32(c0, sa);
+  tmem_ld_wait(sa);
+  tmem_ld32(c0 + 32, sb);
+  softmax_chunk<kMask>(sa, scale2, neg_c2, v0, acc, pk);
+  tmem_st16(col_s + p_col(4 * wg), pk);
+  if (kPSets == 2) {
     tmem_st_wait();
     tc_fence_before();
-    publish_p(p_full_cluster + (2 * t + 1) * 8);
+    publish_p(pbar, set_a);
   }
-  float a0, a1, a2, a3;
-  f2_unpack(acc[0], a0, a1);
-  f2_unpack(acc[1], a2, a3);
-  const float rowsum = (a0 + a1) + (a2 + a3);
+  tmem_ld_wait(sb);
+  softmax_chunk<kMask>(sb, scale2, neg_c2, v0 - 32, acc, pk);
+  tmem_st16(col_s + p_col(4 * wg + 2), pk);
+}
+
+// Stage (j-1) % kKV is free once S of the last query tile for step j is complete: its K was read by
+// the QKs of step j-1 and its V by the PVs of step j-1, all issued before that QK (tcgen05 ops of one
+// thread complete in order). Replaces a tcgen05.commit per step on the MMA thread.
+VOMNI_DEV void release_stage(uint64_t* bars, int j) {
+  if (j > 0) mbar_arrive(&bars[KV_EMPTY + (j - 1) % kKV]);
+}
+
+// Softmax + epilogue warps (warps 2..9). Both warpgroups work on every query tile, in the order the
+// MMA thread produces them (tile 0, tile 1, tile 0, ...): warpgroup wg = (warp-2)/4 takes keys
+// [64wg, 64wg + 64) of each 128-key step and, in the epilogue, output columns [64wg, 64wg + 64).
+// Two warps per SMSP on the same tile hide each other's TMEM and MUFU latencies. quad = warp % 4
+// is the TMEM lane quadrant: thread (quad, lane) owns query row quad*32 + lane of both tiles.
+// q_base: first query row of this CTA's tile 0; tile_stride: rows between its tiles. pbar: the
+// shared::cluster address of the leader's P barriers. lsum: 2 x 2 x 128 floats of shared memory for
+// the row-sum exchange.
+VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort_flag, uint32_t tbase, int warp, int lane,
+                            int q_base, int tile_stride, int bh, int n_tiles, uint32_t pbar, float* lsum) {
+  const int wg = (warp - 2) >> 2;
+  const int quad = warp & 3;
+  const int row = quad * 32 + lane;
+  const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+  const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+  int grow[kQT];
+  bool row_ok[kQT];
+  float c[kQT];
+  uint64_t neg_c2[kQT];
+#pragma unroll
+  for (int t = 0; t < kQT; ++t) {
+    grow[t] = q_base + t * tile_stride + row;
+    row_ok[t] = grow[t] < p.s_q;
+    c[t] = 0.f;
+    if (row_ok[t]) {
+      // c_i = scale * sqrt(kmax2 * ||q_i||^2), held in bf16 like the reference's c_row
+      // (ring_attention_const_max_fwd.py:585-591).
+      const float c32 = p.scale * sqrtf(p.kmax2[bh] * p.qn2[static_cast<size_t>(bh) * p.s_q + grow[t]]);
+      c[t] = __bfloat162float(__float2bfloat16_rn(c32));
+    }
+    const float neg_c = -c[t] * 1.4426950408889634f;
+    neg_c2[t] = f2_pack(neg_c, neg_c);
+  }
+  // One thread frees the K/V stages when S of the last tile of step j is complete: every QK of step
+  // j (and, issued before it, every PV of step j-1) has then finished reading them.
+  const bool releaser = wg == 0 && row == 0;
+  float acc[kQT][4] = {};  // per tile: four fp32 partial row sums
+  bool ok = true;
+  for (int j = 0; j < n_tiles && ok; ++j) {
+    const int valid = p.n_keys - j * kTile;  // keys of this step inside the pass's range
+#pragma unroll
+    for (int t = 0; t < kQT; ++t) {
+      if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+      tc_fence_after();
+      if (releaser && t == kQT - 1) release_stage(bars, j);
+      const uint32_t col_s = tbase + lane_addr + kColS + t * 128;
+      if (valid >= kTile)
+        softmax_share<false>(col_s, wg, scale2, neg_c2[t], valid, acc[t], pbar, 2 * t);
+      else
+        softmax_share<true>(col_s, wg, scale2, neg_c2[t], valid, acc[t], pbar, 2 * t);
+      tmem_st_wait();
+      tc_fence_before();
+      publish_p(pbar, 2 * t + 1);
+    }
+  }
   // ---------------------------------------------------------- epilogue
-  if (ok && mbar_wait(&bars[O_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) {
+  // Row sums of the two warpgroups' key halves meet in shared memory (added in a fixed order, so
+  // results do not depend on scheduling). Every softmax thread reaches the named barrier: all the
+  // waits above are bounded, so an aborted CTA gets here too.
+#pragma unroll
+  for (int t = 0; t < kQT; ++t) {
+    lsum[(t * 2 + wg) * 128 + row] = (acc[t][0] + acc[t][1]) + (acc[t][2] + acc[t][3]);
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(128 * kQT) : "memory");
+  if (!ok) return;
+  const bool acc_in = p.flags & VOMNI_CM_ACC_IN;
+  const bool final_pass = p.flags & VOMNI_CM_FINAL;
+#pragma unroll 1
+  for (int t = 0; t < kQT; ++t) {
+    if (!mbar_wait(&bars[O_FULL + t], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) return;
     tc_fence_after();
     // A pass launched as a programmatic dependent of the previous pass reads and writes acc / out
     // only from here on, after that pass has completed.
-    pdl_wait();
-    const bool acc_in = p.flags & VOMNI_CM_ACC_IN;
-    const bool final_pass = p.flags & VOMNI_CM_FINAL;
-    float l = rowsum;
-    if (acc_in && row_ok) l += p.acc_l[rowidx];
+    if (t == 0) pdl_wait();
+    const size_t rowidx = static_cast<size_t>(bh) * p.s_q + grow[t];
+    float l = lsum[(t * 2) * 128 + row] + lsum[(t * 2 + 1) * 128 + row];
+    if (acc_in && row_ok[t]) l += p.acc_l[rowidx];
     const float inv = 1.f / fmaxf(l, 1e-37f);
     float* acc_row = p.acc_o ? p.acc_o + rowidx * kD : nullptr;
+    const uint32_t col_o = tbase + lane_addr + kColO + t * 128;
 #pragma unroll 1
-    for (int ch = 0; ch < 4; ++ch) {
+    for (int ch = 2 * wg; ch < 2 * wg + 2; ++ch) {
       uint32_t o[32];
       tmem_ld32(col_o + ch * 32, o);
       tmem_ld_wait(o);
-      if (!row_ok) continue;
+      if (!row_ok[t]) continue;
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]);
@@ -235,7 +289,7 @@ VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort
       } else if (p.flags & VOMNI_CM_OUT_DMAJOR) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(bh) * kD * p.s_q;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) out[static_cast<size_t>(ch * 32 + i) * p.s_q + grow] = __float2bfloat16_rn(v[i] * inv);
+        for (int i = 0; i < 32; ++i) out[static_cast<size_t>(ch * 32 + i) * p.s_q + grow[t]] = __float2bfloat16_rn(v[i] * inv);
       } else {
         uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + rowidx * kD + ch * 32);
 #pragma unroll
@@ -249,12 +303,12 @@ VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort
         }
       }
     }
-    if (row_ok) {
+    if (wg == 0 && row_ok[t]) {
       if (!final_pass) {
         p.acc_l[rowidx] = l;
       } else if (p.flags & VOMNI_CM_LSE) {
         const int groups = (p.s_q + 127) / 128;
-        p.lse[(static_cast<size_t>(bh) * 128 + (grow & 127)) * groups + (grow >> 7)] = c + logf(fmaxf(l, 1e-37f));
+        p.lse[(static_cast<size_t>(bh) * 128 + (grow[t] & 127)) * groups + (grow[t] >> 7)] = c[t] + logf(fmaxf(l, 1e-37f));
       }
     }
   }
@@ -274,9 +328,10 @@ constexpr uint32_t kPairKBytes = 64 * kD * 2;   // 16 KB: 64 keys x 128 dims
 constexpr uint32_t kPairVBytes = kTile * 64 * 2;  // 16 KB: 128 keys x 64 dims
 constexpr uint32_t kPairSmemQ = 0;
 constexpr uint32_t kPairSmemK = kPairSmemQ + kQT * kTileBytes;
-constexpr uint32_t kPairSmemV = kPairSmemK + 2 * kPairKBytes;
-constexpr uint32_t kPairSmemBar = kPairSmemV + 2 * kPairVBytes;
-constexpr uint32_t kPairSmemBytes = kPairSmemBar + 256 + 1024;
+constexpr uint32_t kPairSmemV = kPairSmemK + kKV * kPairKBytes;  // V stage i right after all K stages
+constexpr uint32_t kPairSmemBar = kPairSmemV + kKV * kPairVBytes;
+constexpr uint32_t kPairSmemLsum = kPairSmemBar + 256;              // [2 tiles][2 warpgroups][128] fp32
+constexpr uint32_t kPairSmemBytes = kPairSmemLsum + kQT * 2 * 128 * 4 + 1024;
 constexpr uint32_t kIdescQKPair = idesc_bf16(256, 128, false);
 constexpr uint32_t kIdescPVPair = idesc_bf16(256, 128, true);
 
@@ -288,11 +343,15 @@ __device__ __forceinline__ void issue_qk_pair(uint32_t d_s, uint64_t q_desc, uin
     mma_f16_ss_pair(d_s, q_desc + offa, k_desc + offb, kIdescQKPair, kk > 0);
   }
 }
-__device__ __forceinline__ void issue_pv_pair_half(uint32_t d_o, uint32_t p_tmem, uint64_t v_desc, int hf, bool accumulate) {
+// O_t += P_t V over the 16-key groups kk of chunk set `hf`: hf = 0 takes the first 32-key chunk of
+// each warpgroup (kk 0, 1, 4, 5), hf = 1 the second (kk 2, 3, 6, 7). P from TMEM (p_col), V as an
+// MN-major SW128 operand (16 keys = two 8-row groups = +2048 B).
+template <int kSet>
+__device__ __forceinline__ void issue_pv_pair_chunks(uint32_t d_o, uint32_t s_tmem, uint64_t v_desc, uint32_t acc_first) {
 #pragma unroll
-  for (int k2 = 0; k2 < 4; ++k2) {
-    const int kk = hf * 4 + k2;
-    mma_f16_ts_pair(d_o, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPVPair, (accumulate || kk > 0) ? 1u : 0u);
+  for (int i = 0; i < 4; ++i) {
+    const int kk = (i & 1) + (i >> 1) * 4 + kSet * 2;
+    mma_f16_ts_pair(d_o, s_tmem + p_col(kk), v_desc + ((kk * 2048) >> 4), kIdescPVPair, (kSet > 0 || i > 0) ? 1u : acc_first);
   }
 }
 
@@ -318,17 +377,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bars[Q_FULL], 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[K_FULL + i], 1);
-      mbar_init(&bars[K_EMPTY + i], 1);
-      mbar_init(&bars[V_FULL + i], 1);
-      mbar_init(&bars[V_EMPTY + i], 1);
+    for (int i = 0; i < kKV; ++i) {
+      mbar_init(&bars[KV_FULL + i], 1);
+      mbar_init(&bars[KV_EMPTY + i], 1);
     }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&bars[S_FULL + i], 1);
-      mbar_init(&bars[P_FULL + i], 8);  // one arrival per softmax warp of both CTAs
-    }
-    mbar_init(&bars[O_FULL], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[P_FULL + i], kPWarps);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[S_FULL + i], 1);
+    for (int t = 0; t < kQT; ++t) mbar_init(&bars[O_FULL + t], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -361,28 +416,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       const bool kv_ready = !p.ready || ready_wait(p.ready, p.ready_epoch, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x20);
       for (int j = 0; kv_ready && j < n_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % kKV;
+        const uint32_t ph = (j / kKV) & 1;
         const int k_row = p.k_start + j * kTile;
-        if (j >= 2 && !mbar_wait(&bars[K_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) break;
-        if (leader) mbar_expect_tx(&bars[K_FULL + st], 2 * kPairKBytes);
-        tma_load_3d_pair(&tmK, lead_bars + (K_FULL + st) * 8, sK + st * kPairKBytes, x0, k_row + rank * 64, b);
-        tma_load_3d_pair(&tmK, lead_bars + (K_FULL + st) * 8, sK + st * kPairKBytes + kPairKBytes / 2, x0 + 64,
+        if (j >= kKV && !mbar_wait(&bars[KV_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) break;
+        if (leader) mbar_expect_tx(&bars[KV_FULL + st], 2 * (kPairKBytes + kPairVBytes));
+        tma_load_3d_pair(&tmK, lead_bars + (KV_FULL + st) * 8, sK + st * kPairKBytes, x0, k_row + rank * 64, b);
+        tma_load_3d_pair(&tmK, lead_bars + (KV_FULL + st) * 8, sK + st * kPairKBytes + kPairKBytes / 2, x0 + 64,
                          k_row + rank * 64, b);
-        if (j >= 2 && !mbar_wait(&bars[V_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x22)) break;
-        if (leader) mbar_expect_tx(&bars[V_FULL + st], 2 * kPairVBytes);
-        tma_load_3d_pair(&tmV, lead_bars + (V_FULL + st) * 8, sV + st * kPairVBytes, x0 + rank * 64, k_row, b);
+        tma_load_3d_pair(&tmV, lead_bars + (KV_FULL + st) * 8, sV + st * kPairVBytes, x0 + rank * 64, k_row, b);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
+    // Order per step j and tile t: PV_t(j-1) in its two chunk sets, then QK_t(j), which overwrites
+    // S_t / P_t that those PVs read (tcgen05.mma ops of one thread execute in issue order); the tiles
+    // alternate so that one tile's MMAs run while the softmax warps work on the other. The tensor
+    // pipe queues about one MMA, so every wait here is idle tensor time: K and V share one barrier
+    // per stage.
     if (leader && lane == 0) {
       const uint64_t q_desc = make_sdesc(smem_u32(sQ), 16, 1024, kLayoutSW128);
       const uint64_t k_desc = make_sdesc(smem_u32(sK), 16, 1024, kLayoutSW128);
       const uint64_t v_desc = make_sdesc(smem_u32(sV), kPairVBytes, 1024, kLayoutSW128);
       constexpr uint64_t kTileDesc = kTileBytes >> 4;
       bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x23) &&
-                mbar_wait(&bars[K_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24);
+                mbar_wait(&bars[KV_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < kQT; ++t) {
@@ -390,30 +448,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_commit_pair(&bars[S_FULL + 2 * t]);
         }
       }
+      // stage indices advance with the step instead of being recomputed (vs = (j-1) % kKV, ks = j % kKV)
+      int vs = 0, ks = 1 % kKV;
+      uint32_t kv_phase = kKV == 1 ? 1u : 0u;  // parity of the KV_FULL phase of step j (stage ks)
       for (int j = 1; ok && j <= n_tiles; ++j) {
-        const int jj = j - 1;
-        const int vs = jj & 1, ks = j & 1;
-        for (int t = 0; t < kQT && ok; ++t) {
+        const uint32_t pphase = (j - 1) & 1;
+        const uint32_t acc_first = j > 1 ? 1u : 0u;
+        const uint64_t vd = v_desc + ((vs * kPairVBytes) >> 4);
+        const uint64_t kd = k_desc + ((ks * kPairKBytes) >> 4);
+#pragma unroll
+        for (int t = 0; t < kQT; ++t) {
           const uint32_t d_o = tbase + kColO + t * 128, d_s = tbase + kColS + t * 128;
-          for (int hf = 0; hf < 2 && ok; ++hf) {
-            if (!mbar_wait(&bars[P_FULL + 2 * t + hf], jj & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
-            if (t == 0 && hf == 0 && !mbar_wait(&bars[V_FULL + vs], (jj >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x26)) { ok = false; break; }
+          if (kPSets == 2) {
+            if (!mbar_wait(&bars[P_FULL + 2 * t], pphase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
             tc_fence_after();
-            issue_pv_pair_half(d_o, d_s, v_desc + ((vs * kPairVBytes) >> 4), hf, jj > 0);
+            issue_pv_pair_chunks<0>(d_o, d_s, vd, acc_first);
           }
-          if (!ok) break;
+          if (!mbar_wait(&bars[P_FULL + 2 * t + 1], pphase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
+          tc_fence_after();
+          if (kPSets == 1) issue_pv_pair_chunks<0>(d_o, d_s, vd, acc_first);
+          issue_pv_pair_chunks<1>(d_o, d_s, vd, acc_first);
           if (j < n_tiles) {
-            if (t == 0 && !mbar_wait(&bars[K_FULL + ks], (j >> 1) & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24)) { ok = false; break; }
+            if (t == 0 && !mbar_wait(&bars[KV_FULL + ks], kv_phase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24)) { ok = false; break; }
             tc_fence_after();
-            issue_qk_pair(d_s, q_desc + t * kTileDesc, k_desc + ((ks * kPairKBytes) >> 4));
+            issue_qk_pair(d_s, q_desc + t * kTileDesc, kd);
             tc_commit_pair(&bars[S_FULL + 2 * t]);
           }
         }
+        vs = vs + 1 == kKV ? 0 : vs + 1;
+        if (++ks == kKV) {
+          ks = 0;
+          kv_phase ^= 1u;
+        }
       }
-      tc_commit_pair(&bars[O_FULL]);
+      for (int t = 0; t < kQT; ++t) tc_commit_pair(&bars[O_FULL + t]);
     }
   } else {
-    softmax_role(p, bars, abort_flag, tbase, warp, lane, q_base, 2 * kTile, bh, n_tiles, lead_bars + P_FULL * 8);
+    softmax_role(p, bars, abort_flag, tbase, warp, lane, q_base, 2 * kTile, bh, n_tiles, lead_bars + P_FULL * 8,
+                 reinterpret_cast<float*>(smem + kPairSmemLsum));
   }
 
   tc_fence_before();

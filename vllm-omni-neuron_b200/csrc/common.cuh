@@ -406,6 +406,13 @@ VOMNI_DEV void exp2_poly2(float x0, float x1, float& p0, float& p1) {
   p0 = x0 > -125.5f ? r0 : 0.f;
   p1 = x1 > -125.5f ? r1 : 0.f;
 }
+// a += bf16 lo half of `pk`, b += bf16 hi half, exactly (sm_100 mixed-precision add: the bf16 operand
+// is widened exactly, the sum rounded once to fp32) — one instruction per value.
+VOMNI_DEV void add_bf16x2_f32(float& a, float& b, uint32_t pk) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tadd.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
+      : "+f"(a), "+f"(b)
+      : "r"(pk));
+}
 // Two fp32 -> packed bf16x2 (round to nearest even); `lo` lands in bits 0-15.
 VOMNI_DEV uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;

@@ -284,79 +284,87 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // output inside its NKI kernel, one scale per token over the token's N*D values (ROW), then runs the
 // FP8 GEMM. This kernel does the quantisation with the ROW rule of the in-tree NKI ROW quantiser
 // (scale = max(amax / 448, 1e-6), codes = e4m3fn(x * (1 / scale)), adaln_quant.py:520-536) and
-// writes token rows, so the FP8 ROW GEMM of the QKV projection consumes them unchanged. A CTA takes
-// kTok tokens of one batch element: 16-byte loads along the tokens of each of the K rows into shared
-// memory (stored token-major, rows padded so the later column reads hit distinct banks), a |max|
-// per token over K, then 16-byte code stores along K. The d-major input is read once.
-constexpr int kQuantTok = 8;
+// writes token rows, so the FP8 ROW GEMM of the QKV projection consumes them unchanged.
+// A CTA owns kQuantTok consecutive tokens of one batch element and sweeps their K rows twice, each
+// row a 128-byte coalesced read: sweep 1 reduces every token's |max|, sweep 2 (mostly L2 hits: the
+// CTAs in flight hold ~100 MB) stages 64-row slabs in shared memory, transposes them and writes the
+// e4m3 codes as 64-byte runs of token rows.
+constexpr int kQuantTok = 64;
 constexpr int kQuantThreads = 256;
-constexpr int kQuantPad = 8;  // bf16 elements of row padding: 16-byte aligned rows, 4-bank row offset
-constexpr int kQuantUnroll = 8;
+constexpr int kQuantSlab = 64;                 // K rows per sweep-2 slab
+constexpr int kQuantLd = kQuantTok + 2;        // slab row pitch (bf16): 33 words, conflict-free columns
 __global__ void __launch_bounds__(kQuantThreads) oproj_rowquant_kernel(const __nv_bfloat16* __restrict__ attn, int K, int S,
                                                                       uint8_t* __restrict__ codes,
                                                                       float* __restrict__ scales) {
-  extern __shared__ __align__(16) uint8_t smem_q[];
-  const int ld = K + kQuantPad;
-  __nv_bfloat16* sx = reinterpret_cast<__nv_bfloat16*>(smem_q);                  // [kTok][K + pad]
-  float* red = reinterpret_cast<float*>(smem_q + static_cast<size_t>(kQuantTok) * ld * 2);  // [slices][kTok]
-  float* sinv = red + kQuantThreads;                                              // [kTok]
+  __shared__ float red[kQuantThreads / 8][kQuantTok];       // sweep-1 partial maxima
+  __shared__ float sinv[kQuantTok];
+  __shared__ __nv_bfloat16 slab[kQuantSlab * kQuantLd];
   const int b = blockIdx.y;
   const int tok0 = blockIdx.x * kQuantTok;
+  const int ntok = min(kQuantTok, S - tok0);  // a multiple of 8 (S % 8 == 0)
   const __nv_bfloat16* src = attn + static_cast<size_t>(b) * K * S + tok0;
-  const bool full = tok0 + kQuantTok <= S;  // S % 8 == 0: a block is either whole or empty past S
-  if (full) {
-    // kQuantUnroll independent 16-byte loads in flight per thread before their shared-memory stores
-    for (int k0 = threadIdx.x; k0 < K; k0 += kQuantThreads * kQuantUnroll) {
-      uint4 v[kQuantUnroll];
+  // sweep 1: thread (rg, v) reads 16-byte vector v (tokens 8v..8v+7) of rows rg, rg + 32, ...
+  const int v = threadIdx.x & 7, rg = threadIdx.x >> 3;
+  const bool vok = 8 * v < ntok;
+  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (vok) {
+#pragma unroll 4
+    for (int k = rg; k < K; k += kQuantThreads / 8) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(k) * S) + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
-      for (int u = 0; u < kQuantUnroll; ++u) {
-        const int k = k0 + u * kQuantThreads;
-        v[u] = k < K ? __ldcs(reinterpret_cast<const uint4*>(src + static_cast<size_t>(k) * S)) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int u = 0; u < kQuantUnroll; ++u) {
-        const int k = k0 + u * kQuantThreads;
-        if (k >= K) break;
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[u]);
-#pragma unroll
-        for (int t = 0; t < kQuantTok; ++t) sx[t * ld + k] = e[t];
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        m[2 * i] = fmaxf(m[2 * i], fabsf(f.x));
+        m[2 * i + 1] = fmaxf(m[2 * i + 1], fabsf(f.y));
       }
     }
   }
-  __syncthreads();
-  if (!full) return;
-  // |max| per token: thread (t, slice) scans every slices-th k of token t
-  constexpr int kSlices = kQuantThreads / kQuantTok;
-  const int tt = threadIdx.x % kQuantTok, sl = threadIdx.x / kQuantTok;
-  float m = 0.f;
-  for (int k = sl; k < K; k += kSlices) m = fmaxf(m, fabsf(__bfloat162float(sx[tt * ld + k])));
-  red[sl * kQuantTok + tt] = m;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[rg][8 * v + i] = m[i];
   __syncthreads();
   if (threadIdx.x < kQuantTok) {
     float a = 0.f;
-    for (int i = 0; i < kSlices; ++i) a = fmaxf(a, red[i * kQuantTok + threadIdx.x]);
+    for (int r = 0; r < kQuantThreads / 8; ++r) a = fmaxf(a, red[r][threadIdx.x]);
     const float scale = fmaxf(a / 448.f, 1e-6f);
     sinv[threadIdx.x] = __frcp_rn(scale);
-    scales[static_cast<size_t>(b) * S + tok0 + threadIdx.x] = scale;
+    if (threadIdx.x < ntok) scales[static_cast<size_t>(b) * S + tok0 + threadIdx.x] = scale;
   }
   __syncthreads();
-  // codes: consecutive threads take consecutive 16-value chunks of one token row
-  const int nchunk = K / 16;
-  for (int i = threadIdx.x; i < kQuantTok * nchunk; i += kQuantThreads) {
-    const int t = i / nchunk, c = i - t * nchunk;
-    const float inv = sinv[t];
-    const uint4* row = reinterpret_cast<const uint4*>(sx + t * ld + c * 16);
-    const uint4 h0 = row[0], h1 = row[1];
-    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&h0);
-    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&h1);
-    uint32_t w[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __nv_bfloat162* q = j < 2 ? a2 + 2 * j : b2 + 2 * (j - 2);
-      const float2 f0 = __bfloat1622float2(q[0]), f1 = __bfloat1622float2(q[1]);
-      w[j] = e4m3x2(f0.x * inv, f0.y * inv) | (static_cast<uint32_t>(e4m3x2(f1.x * inv, f1.y * inv)) << 16);
+  // sweep 2: per 64-row slab, load (thread = row (tid / 4), 16 tokens (tid % 4)), then emit codes
+  // (thread = token (tid / 4), 16 rows (tid % 4)) from the transposed slab.
+  const int lr = threadIdx.x >> 2, lq = threadIdx.x & 3;
+  const float inv = sinv[lr];
+  const bool ld0 = 16 * lq < ntok, ld1 = 16 * lq + 8 < ntok;
+  // the next slab's two vectors are loaded while the current slab is converted
+  uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+  if (ld0) w0 = __ldcs(reinterpret_cast<const uint4*>(src + static_cast<size_t>(lr) * S + 16 * lq));
+  if (ld1) w1 = __ldcs(reinterpret_cast<const uint4*>(src + static_cast<size_t>(lr) * S + 16 * lq) + 1);
+  for (int k0 = 0; k0 < K; k0 += kQuantSlab) {
+    uint32_t* dst = reinterpret_cast<uint32_t*>(slab + lr * kQuantLd + 16 * lq);  // 4-byte aligned rows
+    dst[0] = w0.x; dst[1] = w0.y; dst[2] = w0.z; dst[3] = w0.w;
+    dst[4] = w1.x; dst[5] = w1.y; dst[6] = w1.z; dst[7] = w1.w;
+    __syncthreads();
+    if (k0 + kQuantSlab < K) {
+      const uint4* rowp = reinterpret_cast<const uint4*>(src + static_cast<size_t>(k0 + kQuantSlab + lr) * S + 16 * lq);
+      if (ld0) w0 = __ldcs(rowp);
+      if (ld1) w1 = __ldcs(rowp + 1);
     }
-    __stcs(reinterpret_cast<uint4*>(codes + (static_cast<size_t>(b) * S + tok0 + t) * K) + c, make_uint4(w[0], w[1], w[2], w[3]));
+    if (lr < ntok) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = 16 * lq + 4 * j;
+        const float x0 = __bfloat162float(slab[(r + 0) * kQuantLd + lr]) * inv;
+        const float x1 = __bfloat162float(slab[(r + 1) * kQuantLd + lr]) * inv;
+        const float x2 = __bfloat162float(slab[(r + 2) * kQuantLd + lr]) * inv;
+        const float x3 = __bfloat162float(slab[(r + 3) * kQuantLd + lr]) * inv;
+        w[j] = e4m3x2(x0, x1) | (static_cast<uint32_t>(e4m3x2(x2, x3)) << 16);
+      }
+      __stcs(reinterpret_cast<uint4*>(codes + (static_cast<size_t>(b) * S + tok0 + lr) * K + k0 + 16 * lq),
+             make_uint4(w[0], w[1], w[2], w[3]));
+    }
+    __syncthreads();
   }
 }
 
@@ -426,16 +434,12 @@ extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const voi
 extern "C" int vomni_oproj_rowquant(const void* attn, int b, int k, int s, void* codes, float* scales,
                                     vomni_stream_t stream) {
   if (!attn || !codes || !scales) return VOMNI_EINVAL;
-  if (b <= 0 || k <= 0 || s <= 0 || (k % 16) || (s % 8) || b > 65535) return VOMNI_EBADSHAPE;
-  const size_t smem = static_cast<size_t>(oproj::kQuantTok) * (k + oproj::kQuantPad) * 2 + (oproj::kQuantThreads + oproj::kQuantTok) * 4;
-  if (smem > 227 * 1024) return VOMNI_EBADSHAPE;
+  if (b <= 0 || k <= 0 || s <= 0 || (k % oproj::kQuantSlab) || (s % 8) || b > 65535) return VOMNI_EBADSHAPE;
   if ((reinterpret_cast<uintptr_t>(attn) | reinterpret_cast<uintptr_t>(codes)) & 15) return VOMNI_EALIGN;
   int rc = require_sm100();
   if (rc) return rc;
-  rc = ensure_max_smem(oproj::oproj_rowquant_kernel, static_cast<int>(smem));
-  if (rc) return rc;
   const dim3 grid((s + oproj::kQuantTok - 1) / oproj::kQuantTok, b);
-  oproj::oproj_rowquant_kernel<<<grid, oproj::kQuantThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  oproj::oproj_rowquant_kernel<<<grid, oproj::kQuantThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(attn), k, s, static_cast<uint8_t*>(codes), scales);
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
