@@ -315,8 +315,13 @@ def main():
     tr_path = ROOT / "profiles" / "cm_attend_traffic.json"
     if tr_path.exists() and kern_flops:
         t = json.loads(tr_path.read_text())
-        # DRAM bytes per (token, head) from a small-case ncu capture, scaled to this launch
-        traffic = round(t["dram_bytes_per_token_head"] * s_loc * HEADS)
+        m = t.get("measured_launch", {})
+        if s_loc == 32760 and world == 1 and m:
+            # the C2 launch itself was captured: its DRAM bytes as measured
+            traffic = int(m["dram_bytes_read"]) + int(m["dram_bytes_write"])
+        else:
+            # DRAM bytes per (token, head) of the captured launch, scaled to this launch
+            traffic = round(t["dram_bytes_per_token_head"] * s_loc * HEADS)
     roof = None
     if kern_ms:
         ach = kern_flops / (kern_ms / 1e3) / 1e12

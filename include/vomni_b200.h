@@ -204,7 +204,8 @@ VOMNI_API int vomni_oproj_gemm(const void* attn, int b, int k, int s, const void
                                vomni_stream_t stream);
 /* The activation side of row_mx_o_proj (diffusion/quantization/row_mx_kernels.py:114-138, whose NKI
  * kernel output_projection_cte quantises its input internally): per-token ROW FP8 quantisation of the
- * d-major attention output attn [b, k, s] bf16 (s % 8 == 0, k % 64 == 0, 16-byte aligned), with the
+ * d-major attention output attn [b, k, s] bf16 (s % 8 == 0, k % 64 == 0, k <= 16384 — k <= 8192 when
+ * k % 128 != 0 — 16-byte aligned), with the
  * ROW rule of adaln_quant.py:520-536 (scale = max(amax / 448, 1e-6), codes = e4m3fn(x * (1 / scale)),
  * amax over the token's k values). Writes token rows codes [b * s, k] e4m3 (16-byte aligned) and
  * scales [b * s] fp32, the operands of vomni_qkv_fp8_gemm (row scale = scales, q_dim = kv_dim = 0). */

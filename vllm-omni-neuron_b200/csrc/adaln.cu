@@ -10,8 +10,9 @@
 //          | e4m3fn(y * (1/s)), s = max(amax/range, 1e-6), packed [H codes | 4 bytes fp32 s] (quant row)
 //          | e4m3fn(y / 2^(e-127)), e = clip(max biased exponent of 32 values - 7, 0, 255)  (quant mx32)
 //
-// One 128-thread CTA per row; the row (<= 16384 values) stays in registers, 16-byte vector loads and
-// stores, block reductions through shared memory. HBM-bound: every byte is read or written once.
+// Persistent 128-thread CTAs stream rows (<= 16384 values) through a shared-memory ring filled by
+// bulk async copies; a row's values stay in registers between the passes, block reductions go
+// through shared memory. HBM-bound: every byte is read or written once.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -23,7 +24,7 @@ namespace vomni {
 namespace adaln {
 
 constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / 32;
+constexpr int kWarps = kThreads / 32;  // the block reductions read the four warp partials as one float4
 
 struct Params {
   const __nv_bfloat16* hidden;
@@ -42,7 +43,11 @@ struct Params {
   void* out;        // bf16 [rows, H] | u8 [rows, H+4] | u8 [rows, H]
   void* out_scale;  // row split: fp32 [rows]; mx32: u8 [rows, H/32]
   __nv_bfloat16* residual_out;  // optional
+  int* status;                  // device status word (bounded-wait timeouts)
+  int slots;                    // ring slots, 2..kMaxSlots
 };
+
+constexpr int kMaxSlots = 4;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -54,202 +59,251 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
-// Block-wide reduction; `red` holds kWarps floats. Ends with every thread holding the result.
-template <bool kMax>
+// Block-wide reduction; `red` holds the kWarps (= 4) warp partials, 16-byte aligned. Ends with every
+// thread holding the result (all threads combine the partials in the same order).
 // One __syncthreads per reduction: each reduction of a row writes its own slot of `red`, and
 // consecutive uses of one slot are always separated by another reduction's barrier.
+template <bool kMax>
 __device__ __forceinline__ float block_reduce(float v, float* red) {
   v = kMax ? warp_max(v) : warp_sum(v);
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) red[w] = v;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  float r = red[0];
-#pragma unroll
-  for (int i = 1; i < kWarps; ++i) r = kMax ? fmaxf(r, red[i]) : r + red[i];
-  return r;
+  const float4 r = *reinterpret_cast<const float4*>(red);
+  return kMax ? fmaxf(fmaxf(r.x, r.y), fmaxf(r.z, r.w)) : (r.x + r.y) + (r.z + r.w);
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 a = __bfloat1622float2(p[i]);
-    f[2 * i] = a.x;
-    f[2 * i + 1] = a.y;
-  }
+// sm_100 mixed-precision arithmetic on packed bf16 pairs: the bf16 operand is widened exactly and the
+// result rounded once to fp32, so no separate unpacking instructions are needed.
+// lo = bf16 lo half of `pk` - c, hi = bf16 hi half - c.
+VOMNI_DEV void sub_bf16x2_f32(uint32_t pk, float c, float& lo, float& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tsub.rn.f32.bf16 %0, l, %3;\n\tsub.rn.f32.bf16 %1, h, %3;\n\t}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(pk), "f"(c));
 }
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 u;
-  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-    w[i] = *reinterpret_cast<uint32_t*>(&b);
-  }
-  return u;
+// Both halves of `pk` widened to fp32 (x + (-0) == x for every x, signed zeros included).
+VOMNI_DEV void widen_bf16x2(uint32_t pk, float& lo, float& hi) {
+  lo = -0.f;
+  hi = -0.f;
+  add_bf16x2_f32(lo, hi, pk);
 }
 
-VOMNI_DEV void cp_async16(void* smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-VOMNI_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-VOMNI_DEV void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+constexpr int kSiteRowWait = 0x30;   // a row's bulk copy never completed
+constexpr int kSiteRowDrain = 0x31;  // an aborted CTA's copies still in flight at exit
+constexpr uint32_t kBf16x2NegZero = 0x80008000u;  // (-0, -0): adding it leaves every value unchanged
 
-// NV = 16-byte chunks (8 values) per thread; a row holds up to NV * 128 * 8 values.
-// Persistent: CTA c handles rows c, c + gridDim.x, ...; each thread streams its own chunks of the
-// next kS-1 rows (hidden, and residual) into a kS-slot shared-memory ring with cp.async, so
-// kS-1 rows per CTA are in flight while one is reduced; the modulation vectors stay in registers
-// for as long as consecutive rows share them.
-template <int NV, bool kRes, int kS>
-__global__ void __launch_bounds__(kThreads, NV <= 6 ? 3 : 1) adaln_kernel(const Params p) {
-  extern __shared__ uint4 ring[];  // [kS][H/8] hidden, then [kS][H/8] residual
+// 128 threads per row: thread t owns the 16-byte chunks t, t + 128, ... (NV of them; kFull when they
+// tile the row exactly, so no chunk needs a bounds predicate). Persistent: CTA c handles rows c,
+// c + gridDim.x, ... One thread moves each row (hidden, and residual) into a p.slots-slot shared-memory
+// ring with a single bulk async copy completing on the slot's mbarrier, so p.slots-1 rows per CTA are
+// in flight while one is reduced, and the warps spend their issue slots on arithmetic only. Registers
+// stay at or under 128 for rows up to 6144 values, so four CTAs (16 warps) share an SM.
+// Ring reuse: a slot is refilled at the start of the row after the one that read it; every thread
+// finishes its ring reads before the first barrier of its row, which thread 0 has passed by then.
+template <int NV, bool kRes, bool kFull>
+__global__ void __launch_bounds__(kThreads, NV <= 6 ? 4 : 1) adaln_kernel(const Params p) {
+  extern __shared__ __align__(128) uint4 ring[];  // [slots][H/8] hidden, then [slots][H/8] residual
+  __shared__ __align__(8) uint64_t full[kMaxSlots];
+  __shared__ int abort_flag;
   // Reduction slots, double-buffered by row parity: a row may take a single barrier, and a slot
   // is rewritten only two rows later, after every thread has passed the next row's barrier.
-  __shared__ float red_sq[2][kWarps];       // LayerNorm sum / RMS sum of squares
-  __shared__ float red_stat_v[2][kWarps];   // LayerNorm squared deviations
-  __shared__ float red_max[2][kWarps];      // absmax for the row quant
-  int parity = 0;
+  __shared__ __align__(16) float red_sq[2][kWarps];      // LayerNorm sum / RMS sum of squares
+  __shared__ __align__(16) float red_stat_v[2][kWarps];  // LayerNorm squared deviations
+  __shared__ __align__(16) float red_max[2][kWarps];     // absmax for the row quant
+  if (static_cast<long long>(blockIdx.x) >= p.rows) return;
   const int H = p.H;
   const int nchunk = H >> 3;
-  long long row = blockIdx.x;
-  if (row >= p.rows) return;
-
+  constexpr int nt = kThreads;
   const long long G = gridDim.x;
-  auto issue = [&](long long r, int slot) {
-    if (r < p.rows) {
-      const uint4* hp = reinterpret_cast<const uint4*>(p.hidden + static_cast<size_t>(r) * H);
-      const uint4* rp = kRes ? reinterpret_cast<const uint4*>(p.residual + static_cast<size_t>(r) * H) : nullptr;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int c = threadIdx.x + i * kThreads;
-        if (c < nchunk) {
-          cp_async16(ring + slot * nchunk + c, hp + c);
-          if (kRes) cp_async16(ring + (kS + slot) * nchunk + c, rp + c);
-        }
-      }
-    }
-    cp_async_commit();  // one group per row slot, empty past the end, so wait counts stay uniform
-  };
-#pragma unroll
-  for (int s0 = 0; s0 < kS - 1; ++s0) issue(row + s0 * G, s0);
-  int k = 0;
-  long long cached_mrow = -1;
-  uint4 mul_r[NV], add_r[NV];
-  const uint4 one_bf16x8 = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+  const uint32_t row_bytes = static_cast<uint32_t>(H) * 2u;
+  volatile int* abort = &abort_flag;
+  const int nslot = p.slots;  // ring depth (runtime: 2..kMaxSlots)
 
-  while (row < p.rows) {
-    const long long next = row + G;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nslot; ++s) mbar_init(&full[s], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Thread 0: bring local row kk (global row blockIdx.x + kk * G) into ring slot s (= kk mod nslot).
+  auto issue = [&](long long kk, int s) {
+    const long long r = blockIdx.x + kk * G;
+    if (r >= p.rows) return;
+    mbar_expect_tx(&full[s], kRes ? 2u * row_bytes : row_bytes);
+    bulk_g2s(ring + s * nchunk, p.hidden + static_cast<size_t>(r) * H, row_bytes, &full[s]);
+    if (kRes) bulk_g2s(ring + (nslot + s) * nchunk, p.residual + static_cast<size_t>(r) * H, row_bytes, &full[s]);
+  };
+  if (threadIdx.x == 0) {
+    for (int kk = 0; kk < nslot - 1; ++kk) issue(kk, kk);
+  }
+
+  int parity = 0;
+  long long cached_mrow = -1;
+  // Modulation as packed bf16 pairs, widened where used (it leaves registers for a fourth CTA):
+  // multiplier 1 and shift -0 when absent, so the arithmetic below is exact without them.
+  uint32_t mulw[NV][4];
+  uint32_t addw[NV][4];
+  const float invH = 1.f / static_cast<float>(H);
+  long long k = 0;
+  int slot = 0;        // ring slot of local row k
+  uint32_t phase = 0;  // the mbarrier phase parity of that slot's current use
+  for (long long row = blockIdx.x; row < p.rows; row += G, ++k) {
+    if (threadIdx.x == 0) {
+      fence_proxy_async_smem();  // the generic-proxy reads of the refilled slot happen before this copy
+      issue(k + nslot - 1, slot == 0 ? nslot - 1 : slot - 1);
+    }
+    mbar_wait(&full[slot], phase, abort, p.status, VOMNI_DEV_TIMEOUT_BASE + kSiteRowWait);
     const size_t base = static_cast<size_t>(row) * H;
-    const long long mrow = row / p.rows_per_mod;
-    issue(row + (kS - 1) * G, (k + kS - 1) % kS);  // refill the slot this thread finished with last row
-    cp_async_wait<kS - 1>();                        // groups complete in order: this row has landed
-    const int slot = k % kS;
-    float x[NV][8];
+    const long long mrow = p.rows_per_mod >= p.rows ? 0 : row / p.rows_per_mod;
+
+    // ---- this thread's chunks of the row, as packed bf16 pairs (after the gated residual)
+    uint32_t xw[NV][4];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int cc = threadIdx.x + i * kThreads;
-      if (cc < nchunk) unpack8(ring[slot * nchunk + cc], x[i]);
-      if (kRes) {
-        const int c = cc;
-        float r[8];
-        if (c < nchunk) unpack8(ring[(kS + slot) * nchunk + c], r);
-        if (c < nchunk) {
-          if (p.gate) {
-            const float4* g = reinterpret_cast<const float4*>(p.gate + static_cast<size_t>(mrow) * H + c * 8);
-            const float4 g0 = g[0], g1 = g[1];
-            x[i][0] = __fmul_rn(x[i][0], g0.x); x[i][1] = __fmul_rn(x[i][1], g0.y);
-            x[i][2] = __fmul_rn(x[i][2], g0.z); x[i][3] = __fmul_rn(x[i][3], g0.w);
-            x[i][4] = __fmul_rn(x[i][4], g1.x); x[i][5] = __fmul_rn(x[i][5], g1.y);
-            x[i][6] = __fmul_rn(x[i][6], g1.z); x[i][7] = __fmul_rn(x[i][7], g1.w);
-          }
-          // product and sum rounded separately (no FMA contraction), as the reference computes them
-#pragma unroll
-          for (int j = 0; j < 8; ++j) x[i][j] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(r[j], x[i][j])));
-          reinterpret_cast<uint4*>(p.residual_out + base)[c] = pack8(x[i]);
+      const int c = threadIdx.x + i * nt;
+      const bool in = kFull || c < nchunk;
+      const uint4 hv = in ? ring[slot * nchunk + c] : make_uint4(0, 0, 0, 0);
+      xw[i][0] = hv.x; xw[i][1] = hv.y; xw[i][2] = hv.z; xw[i][3] = hv.w;
+      if (kRes && in) {
+        const uint4 rv = ring[(nslot + slot) * nchunk + c];
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+        float g[8];
+        if (p.gate) {
+          const float4* gp = reinterpret_cast<const float4*>(p.gate + static_cast<size_t>(mrow) * H + c * 8);
+          const float4 g0 = __ldg(gp), g1 = __ldg(gp + 1);
+          g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
         }
-      }
-      if (threadIdx.x + i * kThreads >= nchunk) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[i][j] = 0.f;
+        for (int w = 0; w < 4; ++w) {
+          float lo, hi;
+          widen_bf16x2(xw[i][w], lo, hi);
+          if (p.gate) {  // product and sum rounded separately, as the reference computes them
+            lo = __fmul_rn(lo, g[2 * w]);
+            hi = __fmul_rn(hi, g[2 * w + 1]);
+          }
+          add_bf16x2_f32(lo, hi, rw[w]);  // residual + gate * hidden, rounded once to fp32
+          xw[i][w] = pack_bf16x2(lo, hi);
+        }
+        reinterpret_cast<uint4*>(p.residual_out + base)[c] = make_uint4(xw[i][0], xw[i][1], xw[i][2], xw[i][3]);
       }
     }
     if (mrow != cached_mrow) {
       cached_mrow = mrow;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        const int c = threadIdx.x + i * kThreads;
-        mul_r[i] = (p.mul && c < nchunk) ? reinterpret_cast<const uint4*>(p.mul + static_cast<size_t>(mrow) * H)[c] : one_bf16x8;
-        add_r[i] = (p.add && c < nchunk) ? reinterpret_cast<const uint4*>(p.add + static_cast<size_t>(mrow) * H)[c] : make_uint4(0, 0, 0, 0);
+        const int c = threadIdx.x + i * nt;
+        const bool in = kFull || c < nchunk;
+        uint4 mv = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);  // bf16 (1, 1)
+        uint4 av = make_uint4(kBf16x2NegZero, kBf16x2NegZero, kBf16x2NegZero, kBf16x2NegZero);
+        if (p.mul && in) mv = __ldg(reinterpret_cast<const uint4*>(p.mul + static_cast<size_t>(mrow) * H) + c);
+        if (p.add && in) av = __ldg(reinterpret_cast<const uint4*>(p.add + static_cast<size_t>(mrow) * H) + c);
+        mulw[i][0] = mv.x; mulw[i][1] = mv.y; mulw[i][2] = mv.z; mulw[i][3] = mv.w;
+        addw[i][0] = av.x; addw[i][1] = av.y; addw[i][2] = av.z; addw[i][3] = av.w;
       }
     }
-    // ---- statistics (fp32): per-thread two-pass mean / squared deviations, merged across the row
-    const float invH = 1.f / static_cast<float>(H);
+
+    // ---- statistics (fp32, two-pass mean / squared deviations) and the centred values d
+    float d[NV][8];
     float mean = 0.f, rstd = 1.f;
     if (p.norm == 0) {
       float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < NV; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) sm[j & 3] += x[i][j];
+      for (int i = 0; i < NV; ++i) {
+        add_bf16x2_f32(sm[0], sm[1], xw[i][0]);
+        add_bf16x2_f32(sm[2], sm[3], xw[i][1]);
+        add_bf16x2_f32(sm[0], sm[1], xw[i][2]);
+        add_bf16x2_f32(sm[2], sm[3], xw[i][3]);
+      }
       mean = block_reduce<false>((sm[0] + sm[1]) + (sm[2] + sm[3]), red_sq[parity]) * invH;
-      float m2[4] = {0.f, 0.f, 0.f, 0.f};
+      if (*abort) break;  // uniform: every thread has passed the barrier above
+      uint64_t m2[2] = {0ull, 0ull};
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        if (threadIdx.x + i * kThreads < nchunk) {
+        const bool in = kFull || threadIdx.x + i * nt < nchunk;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float d = x[i][j] - mean;
-            m2[j & 3] = fmaf(d, d, m2[j & 3]);
-          }
+        for (int w = 0; w < 4; ++w) {
+          sub_bf16x2_f32(xw[i][w], mean, d[i][2 * w], d[i][2 * w + 1]);
+          if (!in) d[i][2 * w] = d[i][2 * w + 1] = 0.f;
+          const uint64_t dd = f2_pack(d[i][2 * w], d[i][2 * w + 1]);
+          m2[w & 1] = f2_fma(dd, dd, m2[w & 1]);
         }
       }
-      rstd = rsqrtf(block_reduce<false>((m2[0] + m2[1]) + (m2[2] + m2[3]), red_stat_v[parity]) * invH + p.eps);
-    } else if (p.norm == 1) {
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      float a0, a1, b0, b1;
+      f2_unpack(m2[0], a0, a1);
+      f2_unpack(m2[1], b0, b1);
+      rstd = rsqrtf(block_reduce<false>((a0 + a1) + (b0 + b1), red_stat_v[parity]) * invH + p.eps);
+    } else {
+      uint64_t v2[2] = {0ull, 0ull};
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j & 3] = fmaf(x[i][j], x[i][j], v[j & 3]);
-      rstd = rsqrtf(block_reduce<false>((v[0] + v[1]) + (v[2] + v[3]), red_sq[parity]) * invH + p.eps);
+        for (int w = 0; w < 4; ++w) {
+          widen_bf16x2(xw[i][w], d[i][2 * w], d[i][2 * w + 1]);
+          if (p.norm == 1) {
+            const uint64_t dd = f2_pack(d[i][2 * w], d[i][2 * w + 1]);
+            v2[w & 1] = f2_fma(dd, dd, v2[w & 1]);
+          }
+        }
+      if (p.norm == 1) {
+        float a0, a1, b0, b1;
+        f2_unpack(v2[0], a0, a1);
+        f2_unpack(v2[1], b0, b1);
+        rstd = rsqrtf(block_reduce<false>((a0 + a1) + (b0 + b1), red_sq[parity]) * invH + p.eps);
+      } else {
+        __syncthreads();  // no reduction in this row: the barrier that orders ring reads before refills
+      }
+      if (*abort) break;
     }
-    // ---- normalise + modulate (mul defaults to 1, add to 0)
+
+    // ---- normalise, modulate (y * mul, then + add, each rounded, as the reference computes them);
+    // rstd is 1 without a norm, so every multiply and add here is exact when its operand is absent.
+    const uint64_t rstd2 = f2_pack(rstd, rstd);
     float am[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      float m[8], a[8];
-      unpack8(mul_r[i], m);
-      unpack8(add_r[i], a);
+      const bool in = kFull || threadIdx.x + i * nt < nchunk;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float y = p.norm == 2 ? x[i][j] : (x[i][j] - mean) * rstd;
-        y = fmaf(y, m[j], a[j]);
-        x[i][j] = y;
-        am[j & 3] = fmaxf(am[j & 3], fabsf(y));
+      for (int w = 0; w < 4; ++w) {
+        float lo, hi;
+        float mlo, mhi;
+        widen_bf16x2(mulw[i][w], mlo, mhi);
+        f2_unpack(f2_mul(f2_mul(f2_pack(d[i][2 * w], d[i][2 * w + 1]), rstd2), f2_pack(mlo, mhi)), lo, hi);
+        add_bf16x2_f32(lo, hi, addw[i][w]);
+        if (!in) lo = hi = 0.f;
+        d[i][2 * w] = lo;
+        d[i][2 * w + 1] = hi;
+        am[(2 * w) & 3] = fmaxf(am[(2 * w) & 3], fabsf(lo));
+        am[(2 * w + 1) & 3] = fmaxf(am[(2 * w + 1) & 3], fabsf(hi));
       }
     }
-    float amax = fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3]));
     // ---- quantise + store
     if (p.quant == 0) {
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        const int c = threadIdx.x + i * kThreads;
-        if (c < nchunk) __stcs(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base) + c, pack8(x[i]));
+        const int c = threadIdx.x + i * nt;
+        if (!(kFull || c < nchunk)) continue;
+        const uint4 o = make_uint4(pack_bf16x2(d[i][0], d[i][1]), pack_bf16x2(d[i][2], d[i][3]),
+                                   pack_bf16x2(d[i][4], d[i][5]), pack_bf16x2(d[i][6], d[i][7]));
+        __stcs(reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + base) + c, o);
       }
     } else if (p.quant == 1) {
-      amax = block_reduce<true>(amax, red_max[parity]);
+      const float amax = block_reduce<true>(fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3])), red_max[parity]);
       const float scale = fmaxf(amax / p.fp8_range, 1e-6f);
       // codes = y * (1 / scale), the reciprocal-multiply of the reference kernel (adaln_quant.py:520-536)
       const float inv = __frcp_rn(scale);
+      const uint64_t inv2 = f2_pack(inv, inv);
       uint8_t* orow = static_cast<uint8_t*>(p.out) + static_cast<size_t>(row) * (p.packed ? H + 4 : H);
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        const int c = threadIdx.x + i * kThreads;
-        if (c >= nchunk) continue;
-        const uint32_t w0 = e4m3x2(x[i][0] * inv, x[i][1] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][2] * inv, x[i][3] * inv)) << 16);
-        const uint32_t w1 = e4m3x2(x[i][4] * inv, x[i][5] * inv) | (static_cast<uint32_t>(e4m3x2(x[i][6] * inv, x[i][7] * inv)) << 16);
+        const int c = threadIdx.x + i * nt;
+        if (!(kFull || c < nchunk)) continue;
+        uint32_t q[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          float lo, hi;
+          f2_unpack(f2_mul(f2_pack(d[i][2 * w], d[i][2 * w + 1]), inv2), lo, hi);
+          q[w] = e4m3x2(lo, hi);
+        }
+        const uint32_t w0 = q[0] | (q[1] << 16), w1 = q[2] | (q[3] << 16);
         if (p.packed) {  // rows are only 4-byte aligned (H + 4 bytes)
           reinterpret_cast<uint32_t*>(orow + c * 8)[0] = w0;
           reinterpret_cast<uint32_t*>(orow + c * 8)[1] = w1;
@@ -268,15 +322,16 @@ __global__ void __launch_bounds__(kThreads, NV <= 6 ? 3 : 1) adaln_kernel(const 
       uint8_t* srow = static_cast<uint8_t*>(p.out_scale) + static_cast<size_t>(row) * (H >> 5);
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        const int c = threadIdx.x + i * kThreads;
+        const int c = threadIdx.x + i * nt;
+        const bool in = kFull || c < nchunk;
         int e = 0;
-        if (c < nchunk) {
+        if (in) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) e = max(e, static_cast<int>((__float_as_uint(x[i][j]) >> 23) & 0xFF));
+          for (int j = 0; j < 8; ++j) e = max(e, static_cast<int>((__float_as_uint(d[i][j]) >> 23) & 0xFF));
         }
         e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
         e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
-        if (c >= nchunk) continue;
+        if (!in) continue;
         const int su = min(max(e - 7, 0), 255);
         // y / 2^(su - 127) as two exact power-of-two multiplies (each factor a normal fp32).
         const int sh = 127 - su;  // in [-128, 127]
@@ -285,25 +340,48 @@ __global__ void __launch_bounds__(kThreads, NV <= 6 ? 3 : 1) adaln_kernel(const 
         const float fb = __uint_as_float(static_cast<uint32_t>(sb + 127) << 23);
         float q[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) q[j] = fminf(fmaxf((x[i][j] * fa) * fb, -448.f), 448.f);
+        for (int j = 0; j < 8; ++j) q[j] = fminf(fmaxf((d[i][j] * fa) * fb, -448.f), 448.f);
         const uint32_t w0 = e4m3x2(q[0], q[1]) | (static_cast<uint32_t>(e4m3x2(q[2], q[3])) << 16);
         const uint32_t w1 = e4m3x2(q[4], q[5]) | (static_cast<uint32_t>(e4m3x2(q[6], q[7])) << 16);
         reinterpret_cast<uint2*>(orow)[c] = make_uint2(w0, w1);
         if ((c & 3) == 0) srow[c >> 2] = static_cast<uint8_t>(su);
       }
     }
-    row = next;
     parity ^= 1;
-    ++k;
+    if (++slot == nslot) {
+      slot = 0;
+      phase ^= 1;
+    }
   }
-  cp_async_wait<0>();  // no copy into shared memory may outlive the CTA
+  // An aborted CTA may still have copies in flight into its ring: rows k .. k + nslot - 1 were issued
+  // when it gave up at row k. Wait for them (bounded) before the shared memory is released. A normal
+  // exit has consumed every row it issued.
+  if (*abort && threadIdx.x == 0) {
+    int s = slot;
+    uint32_t ph = phase;
+    for (long long kk = k; kk < k + nslot; ++kk) {
+      if (blockIdx.x + kk * G >= p.rows) break;
+      int ignored = 0;
+      if (!mbar_wait(&full[s], ph, &ignored, p.status, VOMNI_DEV_TIMEOUT_BASE + kSiteRowDrain)) break;
+      if (++s == nslot) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+  }
 }
 
-template <int NV, int kS>
-int launch_s(const Params& p, cudaStream_t st) {
-  // Persistent grid: as many CTAs as fit on the device at once, each streaming rows through its ring.
-  auto kern = p.residual ? adaln_kernel<NV, true, kS> : adaln_kernel<NV, false, kS>;
-  const size_t smem = static_cast<size_t>(kS) * p.H * 2 * (p.residual ? 2 : 1);
+// Ring slots: four while four CTAs of them fit on an SM (a slot holds one row of hidden, and one of
+// residual), three while three CTAs fit, else two. Persistent grid: as many CTAs as fit on the device
+// at once, each streaming rows through its ring.
+template <int NV>
+int launch_nv(Params p, cudaStream_t st) {
+  const bool full = (p.H >> 3) == NV * kThreads;
+  const size_t slot_bytes = static_cast<size_t>(p.H) * 2 * (p.residual ? 2 : 1);
+  p.slots = 4 * slot_bytes <= 56 * 1024 ? 4 : (3 * slot_bytes <= 72 * 1024 ? 3 : 2);
+  auto kern = p.residual ? (full ? adaln_kernel<NV, true, true> : adaln_kernel<NV, true, false>)
+                         : (full ? adaln_kernel<NV, false, true> : adaln_kernel<NV, false, false>);
+  const size_t smem = static_cast<size_t>(p.slots) * slot_bytes;
   int rc = ensure_max_smem(kern, static_cast<int>(smem));
   if (rc) return rc;
   int per_sm = 0;
@@ -316,11 +394,26 @@ int launch_s(const Params& p, cudaStream_t st) {
   return VOMNI_OK;
 }
 
-// Four ring slots while they fit in 80 KB per CTA, else two.
-template <int NV>
 int launch(const Params& p, cudaStream_t st) {
-  const size_t row_bytes = static_cast<size_t>(p.H) * 2 * (p.residual ? 2 : 1);
-  return 4 * row_bytes <= 80 * 1024 ? launch_s<NV, 4>(p, st) : launch_s<NV, 2>(p, st);
+  switch (((p.H >> 3) + kThreads - 1) / kThreads) {  // NV: chunks per thread, 1..16 for H <= 16384
+    case 1: return launch_nv<1>(p, st);
+    case 2: return launch_nv<2>(p, st);
+    case 3: return launch_nv<3>(p, st);
+    case 4: return launch_nv<4>(p, st);
+    case 5: return launch_nv<5>(p, st);
+    case 6: return launch_nv<6>(p, st);
+    case 7: return launch_nv<7>(p, st);
+    case 8: return launch_nv<8>(p, st);
+    case 9: return launch_nv<9>(p, st);
+    case 10: return launch_nv<10>(p, st);
+    case 11: return launch_nv<11>(p, st);
+    case 12: return launch_nv<12>(p, st);
+    case 13: return launch_nv<13>(p, st);
+    case 14: return launch_nv<14>(p, st);
+    case 15: return launch_nv<15>(p, st);
+    case 16: return launch_nv<16>(p, st);
+    default: return VOMNI_EBADSHAPE;
+  }
 }
 
 }  // namespace adaln
@@ -363,25 +456,7 @@ extern "C" int vomni_adaln_modulate(const void* hidden, const void* residual, co
   p.out = out;
   p.out_scale = out_scale;
   p.residual_out = static_cast<__nv_bfloat16*>(residual_out);
+  p.status = device_status_ptr();
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int nv = (h / 8 + adaln::kThreads - 1) / adaln::kThreads;
-  switch (nv) {
-    case 1: return adaln::launch<1>(p, st);
-    case 2: return adaln::launch<2>(p, st);
-    case 3: return adaln::launch<3>(p, st);
-    case 4: return adaln::launch<4>(p, st);
-    case 5: return adaln::launch<5>(p, st);
-    case 6: return adaln::launch<6>(p, st);
-    case 7: return adaln::launch<7>(p, st);
-    case 8: return adaln::launch<8>(p, st);
-    case 9: return adaln::launch<9>(p, st);
-    case 10: return adaln::launch<10>(p, st);
-    case 11: return adaln::launch<11>(p, st);
-    case 12: return adaln::launch<12>(p, st);
-    case 13: return adaln::launch<13>(p, st);
-    case 14: return adaln::launch<14>(p, st);
-    case 15: return adaln::launch<15>(p, st);
-    case 16: return adaln::launch<16>(p, st);
-    default: return VOMNI_EBADSHAPE;
-  }
+  return adaln::launch(p, st);
 }

@@ -137,6 +137,21 @@ int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t dim0, uint64_
   return r == CUDA_SUCCESS ? VOMNI_OK : VOMNI_ECUDA;
 }
 
+int make_tmap_3d_bf16_plain(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2,
+                            uint32_t box0, uint32_t box1) {
+  int rc = get_encoder();
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (dim0 * 2) % 16) return VOMNI_EALIGN;
+  cuuint64_t dims[3] = {dim0, dim1, dim2};
+  cuuint64_t strides[2] = {dim0 * 2, dim0 * dim1 * 2};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? VOMNI_OK : VOMNI_ECUDA;
+}
+
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
                  uint64_t pitch_bytes, uint32_t box0, uint32_t box1) {
   int rc = get_encoder();

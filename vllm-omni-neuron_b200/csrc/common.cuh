@@ -111,6 +111,16 @@ VOMNI_DEV bool ready_wait(const unsigned* word, unsigned target, volatile int* a
 }
 
 // ---------------------------------------------------------------- TMA (no multicast anywhere)
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory
+// into this CTA's shared memory, completing on `bar` through its transaction count.
+VOMNI_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses (and, through a preceding
+// barrier, other threads') before its later async-proxy ones, e.g. a bulk copy into a reused slot.
+VOMNI_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 VOMNI_DEV void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
@@ -369,6 +379,11 @@ VOMNI_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 VOMNI_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+VOMNI_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
 VOMNI_DEV uint64_t f2_sub(uint64_t a, uint64_t b) {

@@ -35,6 +35,10 @@ int* device_status_ptr();
 // elements apart (0 = dense), box {box0, box1, 1}, 128-byte swizzle, out-of-bounds reads as zero.
 int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2, uint32_t box0,
                       uint32_t box1, uint64_t row_pitch_elems = 0);
+// Rank-3 bf16 tensor map over a dense [dim2][dim1][dim0] tensor without swizzle (boxes land in
+// shared memory as plain row-major [box1][box0]), OOB reads as zero.
+int make_tmap_3d_bf16_plain(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t dim2,
+                            uint32_t box0, uint32_t box1);
 // Rank-2 tensor map over a [dim1][dim0] row-major tensor of 1- or 2-byte elements with an
 // explicit row pitch in bytes, box {box0, box1}, 128-byte swizzle, OOB reads as zero.
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,

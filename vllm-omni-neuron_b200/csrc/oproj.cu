@@ -285,87 +285,116 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // FP8 GEMM. This kernel does the quantisation with the ROW rule of the in-tree NKI ROW quantiser
 // (scale = max(amax / 448, 1e-6), codes = e4m3fn(x * (1 / scale)), adaln_quant.py:520-536) and
 // writes token rows, so the FP8 ROW GEMM of the QKV projection consumes them unchanged.
-// A CTA owns kQuantTok consecutive tokens of one batch element and sweeps their K rows twice, each
-// row a 128-byte coalesced read: sweep 1 reduces every token's |max|, sweep 2 (mostly L2 hits: the
-// CTAs in flight hold ~100 MB) stages 64-row slabs in shared memory, transposes them and writes the
-// e4m3 codes as 64-byte runs of token rows.
-constexpr int kQuantTok = 64;
-constexpr int kQuantThreads = 256;
-constexpr int kQuantSlab = 64;                 // K rows per sweep-2 slab
-constexpr int kQuantLd = kQuantTok + 2;        // slab row pitch (bf16): 33 words, conflict-free columns
-__global__ void __launch_bounds__(kQuantThreads) oproj_rowquant_kernel(const __nv_bfloat16* __restrict__ attn, int K, int S,
-                                                                      uint8_t* __restrict__ codes,
-                                                                      float* __restrict__ scales) {
-  __shared__ float red[kQuantThreads / 8][kQuantTok];       // sweep-1 partial maxima
-  __shared__ float sinv[kQuantTok];
-  __shared__ __nv_bfloat16 slab[kQuantSlab * kQuantLd];
+// A cluster of kCR CTAs owns 32 consecutive tokens of one batch element; CTA r of the cluster holds
+// rows [r*K/kCR, (r+1)*K/kCR) of those tokens in shared memory (TMA boxes of 32 tokens x up to 256
+// rows, 64-byte rows, zero-filled past the sequence end), so the activation crosses HBM once. Each CTA
+// reduces its rows' per-token |max|, the cluster merges the kCR partials through distributed shared
+// memory, and each CTA converts its rows into 32-byte runs of the tokens' code rows.
+constexpr int kRqTok = 32;          // tokens per cluster: one 64-byte box row
+constexpr int kRqThreads = 256;     // 8 warps; lane = token
+constexpr int kRqWarps = kRqThreads / 32;
+constexpr int kRqMaxRows = 2048;    // K rows per CTA (128 KB of shared memory)
+constexpr int kSiteRqLoad = 0x40;   // the CTA's tile loads never completed
+
+VOMNI_DEV float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+template <int kCR>
+__global__ void __cluster_dims__(kCR, 1, 1) __launch_bounds__(kRqThreads)
+    oproj_rowquant_kernel(const __grid_constant__ CUtensorMap tm, int K, int S, int box_rows, uint8_t* __restrict__ codes,
+                          float* __restrict__ scales, int* status) {
+  extern __shared__ __align__(128) __nv_bfloat16 tile[];  // [R][32] bf16
+  __shared__ __align__(8) uint64_t full;
+  __shared__ float red[kRqWarps][kRqTok];
+  __shared__ float part[kRqTok];  // this CTA's per-token |max|, read by the whole cluster
+  __shared__ float sinv[kRqTok];
+  __shared__ int abort_flag;
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int t0 = (blockIdx.x / kCR) * kRqTok;
   const int b = blockIdx.y;
-  const int tok0 = blockIdx.x * kQuantTok;
-  const int ntok = min(kQuantTok, S - tok0);  // a multiple of 8 (S % 8 == 0)
-  const __nv_bfloat16* src = attn + static_cast<size_t>(b) * K * S + tok0;
-  // sweep 1: thread (rg, v) reads 16-byte vector v (tokens 8v..8v+7) of rows rg, rg + 32, ...
-  const int v = threadIdx.x & 7, rg = threadIdx.x >> 3;
-  const bool vok = 8 * v < ntok;
-  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (vok) {
-#pragma unroll 4
-    for (int k = rg; k < K; k += kQuantThreads / 8) {
-      const uint4 w = __ldg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(k) * S) + v);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        m[2 * i] = fmaxf(m[2 * i], fabsf(f.x));
-        m[2 * i + 1] = fmaxf(m[2 * i + 1], fabsf(f.y));
-      }
+  const int R = K / kCR;
+  const int k0 = rank * R;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(&full, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(&full, static_cast<uint32_t>(R) * kRqTok * 2u);
+    for (int r = 0; r < R; r += box_rows) tma_load_3d(&tm, &full, tile + r * kRqTok, t0, k0 + r, b);
+  }
+  const bool loaded = mbar_wait(&full, 0, &abort_flag, status, VOMNI_DEV_TIMEOUT_BASE + kSiteRqLoad);
+  // pass 1: per-token |max| of this CTA's rows on packed bf16 pairs (max of bf16 values is exact).
+  // Half-warp h reads rows 2i + h (32-byte rows of 16 token pairs: the two halves hit disjoint banks),
+  // lane l of it the token pair (2l, 2l + 1); warps stride the row pairs.
+  {
+    const int hw = lane >> 4, pr = lane & 15;
+    const __nv_bfloat162* t2 = reinterpret_cast<const __nv_bfloat162*>(tile);
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.f);
+    for (int r = 2 * warp + hw; r < R; r += 2 * kRqWarps) m2 = __hmax2(m2, __habs2(t2[r * (kRqTok / 2) + pr]));
+    float lo = __low2float(m2), hi = __high2float(m2);
+    lo = fmaxf(lo, __shfl_xor_sync(0xffffffffu, lo, 16));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 16));
+    if (hw == 0) {
+      red[warp][2 * pr] = lo;
+      red[warp][2 * pr + 1] = hi;
     }
   }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) red[rg][8 * v + i] = m[i];
   __syncthreads();
-  if (threadIdx.x < kQuantTok) {
+  if (threadIdx.x < kRqTok) {
+    float a = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < kRqWarps; ++w) a = fmaxf(a, red[w][lane]);
+    part[lane] = a;
+  }
+  cluster_sync();  // every CTA's partials are visible to the cluster
+  if (threadIdx.x < kRqTok) {
     float a = 0.f;
-    for (int r = 0; r < kQuantThreads / 8; ++r) a = fmaxf(a, red[r][threadIdx.x]);
+#pragma unroll
+    for (int q = 0; q < kCR; ++q) a = fmaxf(a, ld_shared_cluster_f32(mapa_shared(smem_u32(&part[lane]), q)));
     const float scale = fmaxf(a / 448.f, 1e-6f);
-    sinv[threadIdx.x] = __frcp_rn(scale);
-    if (threadIdx.x < ntok) scales[static_cast<size_t>(b) * S + tok0 + threadIdx.x] = scale;
+    sinv[lane] = __frcp_rn(scale);
+    if (rank == 0 && t0 + lane < S) scales[static_cast<size_t>(b) * S + t0 + lane] = scale;
   }
   __syncthreads();
-  // sweep 2: per 64-row slab, load (thread = row (tid / 4), 16 tokens (tid % 4)), then emit codes
-  // (thread = token (tid / 4), 16 rows (tid % 4)) from the transposed slab.
-  const int lr = threadIdx.x >> 2, lq = threadIdx.x & 3;
-  const float inv = sinv[lr];
-  const bool ld0 = 16 * lq < ntok, ld1 = 16 * lq + 8 < ntok;
-  // the next slab's two vectors are loaded while the current slab is converted
-  uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
-  if (ld0) w0 = __ldcs(reinterpret_cast<const uint4*>(src + static_cast<size_t>(lr) * S + 16 * lq));
-  if (ld1) w1 = __ldcs(reinterpret_cast<const uint4*>(src + static_cast<size_t>(lr) * S + 16 * lq) + 1);
-  for (int k0 = 0; k0 < K; k0 += kQuantSlab) {
-    uint32_t* dst = reinterpret_cast<uint32_t*>(slab + lr * kQuantLd + 16 * lq);  // 4-byte aligned rows
-    dst[0] = w0.x; dst[1] = w0.y; dst[2] = w0.z; dst[3] = w0.w;
-    dst[4] = w1.x; dst[5] = w1.y; dst[6] = w1.z; dst[7] = w1.w;
-    __syncthreads();
-    if (k0 + kQuantSlab < K) {
-      const uint4* rowp = reinterpret_cast<const uint4*>(src + static_cast<size_t>(k0 + kQuantSlab + lr) * S + 16 * lq);
-      if (ld0) w0 = __ldcs(rowp);
-      if (ld1) w1 = __ldcs(rowp + 1);
-    }
-    if (lr < ntok) {
-      uint32_t w[4];
+  // pass 2: lane = token; a warp turns 32 consecutive rows into one 32-byte run of each token's codes
+  const float inv = sinv[lane];
+  const bool tok_ok = t0 + lane < S;
+  uint8_t* crow = codes + (static_cast<size_t>(b) * S + t0 + lane) * K + k0;
+  for (int c = warp; c * 32 < R; c += kRqWarps) {
+    const int nrow = min(32, R - c * 32);  // 32, or 16 in a last chunk (K % 64 == 0)
+    uint32_t w[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = 16 * lq + 4 * j;
-        const float x0 = __bfloat162float(slab[(r + 0) * kQuantLd + lr]) * inv;
-        const float x1 = __bfloat162float(slab[(r + 1) * kQuantLd + lr]) * inv;
-        const float x2 = __bfloat162float(slab[(r + 2) * kQuantLd + lr]) * inv;
-        const float x3 = __bfloat162float(slab[(r + 3) * kQuantLd + lr]) * inv;
+    for (int j = 0; j < 8; ++j) {
+      const int r = c * 32 + 4 * j;
+      if (4 * j < nrow) {
+        const float x0 = __bfloat162float(tile[(r + 0) * kRqTok + lane]) * inv;
+        const float x1 = __bfloat162float(tile[(r + 1) * kRqTok + lane]) * inv;
+        const float x2 = __bfloat162float(tile[(r + 2) * kRqTok + lane]) * inv;
+        const float x3 = __bfloat162float(tile[(r + 3) * kRqTok + lane]) * inv;
         w[j] = e4m3x2(x0, x1) | (static_cast<uint32_t>(e4m3x2(x2, x3)) << 16);
+      } else {
+        w[j] = 0;
       }
-      __stcs(reinterpret_cast<uint4*>(codes + (static_cast<size_t>(b) * S + tok0 + lr) * K + k0 + 16 * lq),
-             make_uint4(w[0], w[1], w[2], w[3]));
     }
-    __syncthreads();
+    if (tok_ok) {
+      uint4* dst = reinterpret_cast<uint4*>(crow + c * 32);
+      __stcs(dst, make_uint4(w[0], w[1], w[2], w[3]));
+      if (nrow > 16) __stcs(dst + 1, make_uint4(w[4], w[5], w[6], w[7]));
+    }
   }
+  // A CTA whose loads gave up waits once more (bounded) so that no copy into its shared memory
+  // outlives it; every CTA keeps its partials alive until the whole cluster has read them.
+  if (!loaded && threadIdx.x == 0) {
+    int ignored = 0;
+    mbar_wait(&full, 0, &ignored, status, VOMNI_DEV_TIMEOUT_BASE + kSiteRqLoad);
+  }
+  cluster_sync();
 }
 
 int ensure_smem_attr() {
@@ -434,13 +463,28 @@ extern "C" int vomni_oproj_gemm(const void* attn, int b, int k, int s, const voi
 extern "C" int vomni_oproj_rowquant(const void* attn, int b, int k, int s, void* codes, float* scales,
                                     vomni_stream_t stream) {
   if (!attn || !codes || !scales) return VOMNI_EINVAL;
-  if (b <= 0 || k <= 0 || s <= 0 || (k % oproj::kQuantSlab) || (s % 8) || b > 65535) return VOMNI_EBADSHAPE;
+  if (b <= 0 || k <= 0 || s <= 0 || (k % 64) || (s % 8) || b > 65535) return VOMNI_EBADSHAPE;
   if ((reinterpret_cast<uintptr_t>(attn) | reinterpret_cast<uintptr_t>(codes)) & 15) return VOMNI_EALIGN;
   int rc = require_sm100();
   if (rc) return rc;
-  const dim3 grid((s + oproj::kQuantTok - 1) / oproj::kQuantTok, b);
-  oproj::oproj_rowquant_kernel<<<grid, oproj::kQuantThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(attn), k, s, static_cast<uint8_t*>(codes), scales);
+  // Clusters of 8 CTAs (k / 8 rows each: 40 KB at k = 5120, so several CTAs share an SM and their
+  // load and convert phases overlap); 4 when k / 8 would not be a multiple of 16 rows.
+  const int cr = (k % 128 == 0) ? 8 : 4;
+  if (k / cr > oproj::kRqMaxRows) return VOMNI_EBADSHAPE;
+  const int rows = k / cr;  // a multiple of 16
+  int box = 256;
+  while (rows % box) box >>= 1;
+  CUtensorMap tm;
+  rc = make_tmap_3d_bf16_plain(&tm, attn, static_cast<uint64_t>(s), static_cast<uint64_t>(k), static_cast<uint64_t>(b),
+                               oproj::kRqTok, static_cast<uint32_t>(box));
+  if (rc) return rc;
+  const int smem = rows * oproj::kRqTok * 2;
+  auto kern = cr == 4 ? oproj::oproj_rowquant_kernel<4> : oproj::oproj_rowquant_kernel<8>;
+  rc = ensure_max_smem(kern, smem);
+  if (rc) return rc;
+  const dim3 grid(static_cast<unsigned>((s + oproj::kRqTok - 1) / oproj::kRqTok * cr), static_cast<unsigned>(b));
+  kern<<<grid, oproj::kRqThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(tm, k, s, box, static_cast<uint8_t*>(codes),
+                                                                                  scales, device_status_ptr());
   VOMNI_CUDA_TRY(cudaGetLastError());
   return VOMNI_OK;
 }
