@@ -99,7 +99,8 @@ struct Params {
   float* lse;          // [b*h, 128, ceil(s_q/128)]
   int flags;
   int* status;
-  const unsigned* ready;  // if set: K/V of this pass are valid once *ready reaches ready_epoch
+  const unsigned* ready;  // if set: K/V of this pass are valid once ready[0 .. ready_count) reach ready_epoch
+  int ready_count;
   unsigned ready_epoch;
 };
 
@@ -414,7 +415,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_load_3d_pair(&tmQ, lead_bars + Q_FULL * 8, sQ + t * kTileBytes, x0, qr, b);
         tma_load_3d_pair(&tmQ, lead_bars + Q_FULL * 8, sQ + t * kTileBytes + kHalfBytes, x0 + 64, qr, b);
       }
-      const bool kv_ready = !p.ready || ready_wait(p.ready, p.ready_epoch, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x20);
+      bool kv_ready = true;
+      for (int w = 0; p.ready && kv_ready && w < p.ready_count; ++w)
+        kv_ready = ready_wait(p.ready + w, p.ready_epoch, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x20);
       for (int j = 0; kv_ready && j < n_tiles; ++j) {
         const int st = j % kKV;
         const uint32_t ph = (j / kKV) & 1;
@@ -609,13 +612,14 @@ extern "C" int vomni_cm_attend_strided(const void* q, const void* k, const void*
                                        float softmax_scale, const float* qn2, const float* kmax2, float* acc_o,
                                        float* acc_l, int flags, void* out, float* lse, vomni_stream_t stream) {
   return vomni::cm_attend_gated(q, k, v, b, s_q, s_kv, k_start, n_keys, h, d, q_stride, kv_stride, softmax_scale, qn2,
-                                kmax2, acc_o, acc_l, flags, out, lse, nullptr, 0u, stream);
+                                kmax2, acc_o, acc_l, flags, out, lse, nullptr, 0, 0u, stream);
 }
 
 int vomni::cm_attend_gated(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start,
                            int n_keys, int h, int d, long long q_stride, long long kv_stride, float softmax_scale,
                            const float* qn2, const float* kmax2, float* acc_o, float* acc_l, int flags, void* out,
-                           float* lse, const unsigned* ready, unsigned ready_epoch, vomni_stream_t stream) {
+                           float* lse, const unsigned* ready, int ready_count, unsigned ready_epoch,
+                           vomni_stream_t stream) {
   if (!q || !k || !v || !qn2 || !kmax2) return VOMNI_EINVAL;
   if (d != cm::kD || b <= 0 || s_q <= 0 || h <= 0 || n_keys <= 0 || k_start < 0 || k_start + n_keys > s_kv)
     return VOMNI_EBADSHAPE;
@@ -662,6 +666,7 @@ int vomni::cm_attend_gated(const void* q, const void* k, const void* v, int b, i
   p.flags = flags;
   p.status = device_status_ptr();
   p.ready = ready;
+  p.ready_count = ready ? ready_count : 0;
   p.ready_epoch = ready_epoch;
 
   rc = ensure_max_smem(cm::cm_attend_pair_kernel, cm::kPairSmemBytes);

@@ -48,12 +48,12 @@ int make_tmap_2d_plain(CUtensorMap* map, CUtensorMapDataType dtype, const void* 
                        uint64_t pitch_bytes, uint32_t box0, uint32_t box1);
 
 // vomni_cm_attend_strided with an optional in-kernel gate: when `ready` is set, every CTA waits
-// (bounded) for *ready >= ready_epoch before its first K/V load. Used by the ring, whose copy stream
+// (bounded) for ready[0 .. ready_count) >= ready_epoch before its first K/V load. Used by the ring, whose copy stream
 // posts the word after a block's copies, so that no stream-level wait separates consecutive passes.
 int cm_attend_gated(const void* q, const void* k, const void* v, int b, int s_q, int s_kv, int k_start, int n_keys,
                     int h, int d, long long q_stride, long long kv_stride, float softmax_scale, const float* qn2,
                     const float* kmax2, float* acc_o, float* acc_l, int flags, void* out, float* lse,
-                    const unsigned* ready, unsigned ready_epoch, vomni_stream_t stream);
+                    const unsigned* ready, int ready_count, unsigned ready_epoch, vomni_stream_t stream);
 // cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes) once per (kernel, device, size);
 // thread-safe. Kernels above 48 KB of dynamic shared memory need it on every device they run on.
 int ensure_max_smem(const void* func, int bytes);

@@ -8,12 +8,14 @@
 //
 // B200 design: NVSwitch gives every GPU full bandwidth to every peer, so the store-and-forward ring
 // becomes direct pulls: step s copies block (r - s) mod N straight from its owner's registered send
-// buffer into a local gather buffer, on a copy-engine stream (cudaMemcpyAsync between IPC-mapped
-// device memory; no SMs, no TMA on peer memory, no multicast). The attention runs as a few passes
+// buffer into a local gather buffer, on copy-engine streams (cudaMemcpyAsync between IPC-mapped
+// device memory; no SMs, no TMA on peer memory, no multicast). The steps are spread round-robin over
+// kCopyStreams streams so that several peers' blocks are in flight at once (one stream's copies run
+// one after another and leave NVLink bandwidth unused). The attention runs as a few passes
 // over ranges of arrived blocks (local block first, then ranges of 1, 2, 4, ... blocks), accumulating
-// into an fp32 partial; the last pass normalises. After a block's copies the copy stream posts a
+// into an fp32 partial; the last pass normalises. After a block's copies its copy stream posts a
 // per-step ready word (cuStreamWriteValue32, executed by the GPU front end, not by a kernel); each
-// pass waits for its last block's word inside the kernel (bounded), before its first K/V load, so
+// pass waits for the words of all its blocks inside the kernel (bounded), before its first K/V load, so
 // no stream-level wait separates consecutive passes and a pass starts as a programmatic dependent
 // of the previous one, filling the SMs its last wave leaves idle.
 //
@@ -23,7 +25,7 @@
 //    every peer reached it, i.e. finished its earlier stream work;
 //  * send buffers are double-buffered by call parity: a rank rewrites send[p] two calls later, after
 //    the intervening call's all_reduce, by which time every peer's copies of send[p] have completed
-//    (each rank's stream joins its copy stream after the last pass, before it can enter the next
+//    (each rank's stream joins its copy streams after the last pass, before it can enter the next
 //    all_reduce).
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -39,6 +41,13 @@
 
 namespace vomni {
 namespace {
+
+// Copy streams per ring (at most world - 1 are used).
+#ifndef VOMNI_RING_COPY_STREAMS
+#define VOMNI_RING_COPY_STREAMS 4
+#endif
+constexpr int kCopyStreams = VOMNI_RING_COPY_STREAMS;
+static_assert(kCopyStreams >= 1 && kCopyStreams <= 8, "copy streams per ring");
 
 struct NcclApi {
   void* handle = nullptr;
@@ -86,10 +95,13 @@ struct vomni_ring {
   int rank = 0, world = 1, device = 0;
   int b = 0, s_max = 0, h = 0, d = 0;
   ncclComm_t comm = nullptr;
-  cudaStream_t copy_stream = nullptr;
-  cudaEvent_t ev_ready = nullptr;  // recorded on the caller stream after the all_reduce
+  cudaStream_t copy_stream = nullptr;  // copy_streams[0]
+  std::vector<cudaStream_t> copy_streams;
+  cudaEvent_t ev_inputs = nullptr;  // recorded on the caller stream at entry (K/V written)
+  cudaEvent_t ev_sent = nullptr;    // recorded on copy stream 0 after the send-buffer copies
+  cudaEvent_t ev_ready = nullptr;   // recorded on the caller stream after the all_reduce
   std::vector<cudaEvent_t> ev_block;  // copy of ring step s done
-  cudaEvent_t ev_copies_done = nullptr;
+  std::vector<cudaEvent_t> ev_copies_done;  // per copy stream: its last copy done
   unsigned* ready = nullptr;  // [world] device words: ready[s] = call number once step s's block landed
   // Registered send buffer: [parity 2][K|V 2][b, s_max, h, d] bf16 (one allocation, IPC-exported).
   void* send = nullptr;
@@ -126,9 +138,11 @@ void ring_free(vomni_ring* R) {
   if (R->acc_l) cudaFree(R->acc_l);
   if (R->ready) cudaFree(R->ready);
   for (cudaEvent_t e : R->ev_block) cudaEventDestroy(e);
+  for (cudaEvent_t e : R->ev_copies_done) cudaEventDestroy(e);
   if (R->ev_ready) cudaEventDestroy(R->ev_ready);
-  if (R->ev_copies_done) cudaEventDestroy(R->ev_copies_done);
-  if (R->copy_stream) cudaStreamDestroy(R->copy_stream);
+  if (R->ev_inputs) cudaEventDestroy(R->ev_inputs);
+  if (R->ev_sent) cudaEventDestroy(R->ev_sent);
+  for (cudaStream_t cs : R->copy_streams) cudaStreamDestroy(cs);
   if (R->comm) {
     const NcclApi* n = nccl();
     if (n) (R->broken ? n->CommAbort : n->CommDestroy)(R->comm);
@@ -219,9 +233,17 @@ extern "C" int vomni_ring_create(vomni_ring** out, int rank, int world, const vo
   RING_TRY(nccl_check(n->CommInitRank(&R->comm, world, id, rank)));
   const size_t toks = static_cast<size_t>(b) * s_max;
   R->block_bytes = toks * h * d * 2;
-  RING_CUDA(cudaStreamCreateWithFlags(&R->copy_stream, cudaStreamNonBlocking));
+  const int ncs = world > 1 ? (world - 1 < kCopyStreams ? world - 1 : kCopyStreams) : 1;
+  R->copy_streams.resize(ncs, nullptr);
+  R->ev_copies_done.resize(ncs, nullptr);
+  for (int i = 0; i < ncs; ++i) {
+    RING_CUDA(cudaStreamCreateWithFlags(&R->copy_streams[i], cudaStreamNonBlocking));
+    RING_CUDA(cudaEventCreateWithFlags(&R->ev_copies_done[i], cudaEventDisableTiming));
+  }
+  R->copy_stream = R->copy_streams[0];
   RING_CUDA(cudaEventCreateWithFlags(&R->ev_ready, cudaEventDisableTiming));
-  RING_CUDA(cudaEventCreateWithFlags(&R->ev_copies_done, cudaEventDisableTiming));
+  RING_CUDA(cudaEventCreateWithFlags(&R->ev_inputs, cudaEventDisableTiming));
+  RING_CUDA(cudaEventCreateWithFlags(&R->ev_sent, cudaEventDisableTiming));
   R->ev_block.resize(world, nullptr);
   for (int i = 0; i < world; ++i) RING_CUDA(cudaEventCreateWithFlags(&R->ev_block[i], cudaEventDisableTiming));
   RING_CUDA(cudaMalloc(&R->qn2, static_cast<size_t>(b) * h * s_max * sizeof(float)));
@@ -331,79 +353,101 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
   ++R->calls;
   const unsigned epoch = static_cast<unsigned>(R->calls);
   const StreamWriteValue32Fn write_value = stream_write_value32();
+  // Every copy-stream path below ends by joining all copy streams into the caller stream (also on an
+  // error), so no later work on the caller stream can overlap this call's copies. A failure after
+  // the first copy is queued leaves the ring unusable (peers' copies and ready words no longer match
+  // this call), so it also marks the ring broken.
+  const int ncs = static_cast<int>(R->copy_streams.size());
+  auto join_copies = [&](int status) {
+    for (int i = 0; i < ncs; ++i) {
+      cudaError_t e = cudaEventRecord(R->ev_copies_done[i], R->copy_streams[i]);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(st, R->ev_copies_done[i], 0);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        cudaStreamSynchronize(R->copy_streams[i]);  // cannot join by event: wait for the queued copies here
+        if (status == VOMNI_OK) status = VOMNI_ECUDA;
+      }
+    }
+    return status;
+  };
+  auto copies_failed = [&](int status) {
+    R->broken = true;
+    return join_copies(status);
+  };
   // 1. publish this rank's K/V block in its registered send buffer (b blocks of s_loc tokens; the
-  //    buffer keeps an s_max stride per batch so peers address it with the creation-time geometry).
+  //    buffer keeps an s_max stride per batch so peers address it with the creation-time geometry),
+  //    on copy stream 0 while the caller stream computes the norms.
   uint8_t* my_send = static_cast<uint8_t*>(R->send) + static_cast<size_t>(parity) * 2 * R->block_bytes;
   const size_t bstride = static_cast<size_t>(R->s_max) * h * d * 2;
   const size_t src_bstride = static_cast<size_t>(s_loc) * kv_stride * 2;  // a strided view's batch stride
   const size_t row_bytes = static_cast<size_t>(dense) * 2;
+  VOMNI_CUDA_TRY(cudaEventRecord(R->ev_inputs, st));
+  if (const cudaError_t e = cudaStreamWaitEvent(R->copy_stream, R->ev_inputs, 0); e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return VOMNI_ECUDA;
+  }
   for (int bi = 0; bi < b; ++bi) {
-    VOMNI_CUDA_TRY(cudaMemcpy2DAsync(my_send + bi * bstride, row_bytes, static_cast<const uint8_t*>(k) + bi * src_bstride,
-                                     static_cast<size_t>(kv_stride) * 2, row_bytes, s_loc, cudaMemcpyDeviceToDevice, st));
-    VOMNI_CUDA_TRY(cudaMemcpy2DAsync(my_send + R->block_bytes + bi * bstride, row_bytes,
-                                     static_cast<const uint8_t*>(v) + bi * src_bstride, static_cast<size_t>(kv_stride) * 2,
-                                     row_bytes, s_loc, cudaMemcpyDeviceToDevice, st));
+    cudaError_t e = cudaMemcpy2DAsync(my_send + bi * bstride, row_bytes, static_cast<const uint8_t*>(k) + bi * src_bstride,
+                                      static_cast<size_t>(kv_stride) * 2, row_bytes, s_loc, cudaMemcpyDeviceToDevice,
+                                      R->copy_stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(my_send + R->block_bytes + bi * bstride, row_bytes,
+                            static_cast<const uint8_t*>(v) + bi * src_bstride, static_cast<size_t>(kv_stride) * 2, row_bytes,
+                            s_loc, cudaMemcpyDeviceToDevice, R->copy_stream);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return copies_failed(VOMNI_ECUDA);
+    }
   }
-  // 2. local norms, 3. global key max (also the "peers' blocks are published" point)
+  if (const cudaError_t e = cudaEventRecord(R->ev_sent, R->copy_stream); e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return copies_failed(VOMNI_ECUDA);
+  }
+  // 2. local norms, 3. global key max (also the "peers' blocks are published" point: the all_reduce
+  //    follows this rank's send-buffer copies on the caller stream)
   rc = vomni_cm_prologue_strided(q, k, b, s_loc, h, d, q_stride, kv_stride, R->qn2, R->kmax2, stream);
-  if (rc) return rc;
-  if (n->AllReduce(R->kmax2, R->kmax2, static_cast<size_t>(b) * h, ncclFloat32, ncclMax, R->comm, st) != ncclSuccess) {
-    R->broken = true;
-    return VOMNI_ENCCL;
+  if (rc) return copies_failed(rc);
+  if (const cudaError_t e = cudaStreamWaitEvent(st, R->ev_sent, 0); e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return copies_failed(VOMNI_ECUDA);
   }
-  VOMNI_CUDA_TRY(cudaEventRecord(R->ev_ready, st));
-  // 4. direct pulls on the copy stream, in ring order. A failure after the first copy is queued
-  //    leaves the ring unusable (peers' copies and ready words no longer match this call), so it
-  //    marks the ring broken; the caller stream still joins whatever was queued on the copy stream.
-  VOMNI_CUDA_TRY(cudaStreamWaitEvent(R->copy_stream, R->ev_ready, 0));
-  auto pull_failed = [&](int status) {
-    R->broken = true;
-    if (cudaEventRecord(R->ev_copies_done, R->copy_stream) != cudaSuccess ||
-        cudaStreamWaitEvent(st, R->ev_copies_done, 0) != cudaSuccess)
-      cudaStreamSynchronize(R->copy_stream);  // cannot join by event: wait for the queued copies here
-    return status;
-  };
+  if (n->AllReduce(R->kmax2, R->kmax2, static_cast<size_t>(b) * h, ncclFloat32, ncclMax, R->comm, st) != ncclSuccess)
+    return copies_failed(VOMNI_ENCCL);
+  if (const cudaError_t e = cudaEventRecord(R->ev_ready, st); e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return copies_failed(VOMNI_ECUDA);
+  }
+  // 4. direct pulls, ring step s on copy stream (s - 1) % ncs, each step posting its ready word.
+  for (int i = 0; i < ncs; ++i) {
+    if (const cudaError_t e = cudaStreamWaitEvent(R->copy_streams[i], R->ev_ready, 0); e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return copies_failed(VOMNI_ECUDA);
+    }
+  }
   const size_t gstride = static_cast<size_t>(N - 1) * s_loc * h * d * 2;  // per batch in the gather buffer
   for (int s = 1; s < N; ++s) {
+    cudaStream_t cs = R->copy_streams[(s - 1) % ncs];
     const int src = vomni_ring_source_rank(R->rank, N, s);
     const uint8_t* ps = static_cast<const uint8_t*>(R->peer_send[src]) + static_cast<size_t>(parity) * 2 * R->block_bytes;
     for (int bi = 0; bi < b; ++bi) {
       uint8_t* gk = static_cast<uint8_t*>(R->gather_k) + bi * gstride + static_cast<size_t>(s - 1) * blk;
       uint8_t* gv = static_cast<uint8_t*>(R->gather_v) + bi * gstride + static_cast<size_t>(s - 1) * blk;
-      cudaError_t e = cudaMemcpyAsync(gk, ps + bi * bstride, blk, cudaMemcpyDeviceToDevice, R->copy_stream);
-      if (e == cudaSuccess)
-        e = cudaMemcpyAsync(gv, ps + R->block_bytes + bi * bstride, blk, cudaMemcpyDeviceToDevice, R->copy_stream);
+      cudaError_t e = cudaMemcpyAsync(gk, ps + bi * bstride, blk, cudaMemcpyDeviceToDevice, cs);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(gv, ps + R->block_bytes + bi * bstride, blk, cudaMemcpyDeviceToDevice, cs);
       if (e != cudaSuccess) {
         set_last_cuda_error(e);
-        return pull_failed(VOMNI_ECUDA);
+        return copies_failed(VOMNI_ECUDA);
       }
     }
-    const cudaError_t e = cudaEventRecord(R->ev_block[s], R->copy_stream);
-    if (e != cudaSuccess) {
+    if (const cudaError_t e = cudaEventRecord(R->ev_block[s], cs); e != cudaSuccess) {
       set_last_cuda_error(e);
-      return pull_failed(VOMNI_ECUDA);
+      return copies_failed(VOMNI_ECUDA);
     }
-    if (write_value && write_value(reinterpret_cast<CUstream>(R->copy_stream),
-                                   reinterpret_cast<CUdeviceptr>(R->ready + s), epoch, 0) != CUDA_SUCCESS)
-      return pull_failed(VOMNI_ECUDA);
-  }
-  if (const cudaError_t e = cudaEventRecord(R->ev_copies_done, R->copy_stream); e != cudaSuccess) {
-    set_last_cuda_error(e);
-    R->broken = true;
-    cudaStreamSynchronize(R->copy_stream);
-    return VOMNI_ECUDA;
+    if (write_value && write_value(reinterpret_cast<CUstream>(cs), reinterpret_cast<CUdeviceptr>(R->ready + s), epoch, 0) !=
+                           CUDA_SUCCESS)
+      return copies_failed(VOMNI_ECUDA);
   }
   // 5. passes: local block, then ranges of arrived blocks; fp32 partial, normalise on the last.
-  // Every return from here joins the copy stream first (also on an error), so no later work on the
-  // caller stream can overlap this call's copies.
-  auto join_copies = [&](int status) {
-    const cudaError_t e = cudaStreamWaitEvent(st, R->ev_copies_done, 0);
-    if (status == VOMNI_OK && e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return static_cast<int>(VOMNI_ECUDA);
-    }
-    return status;
-  };
   int first[64], count[64];
   const int np = vomni_ring_phase_plan(N, first, count, 64);
   if (np < 2) return join_copies(VOMNI_EINVAL);
@@ -412,25 +456,27 @@ extern "C" int vomni_ring_attention_strided(vomni_ring* R, const void* q, const 
   if (rc) return join_copies(rc);
   const int s_kv = (N - 1) * s_loc;
   for (int p = 1; p < np; ++p) {
-    const int last_step = first[p] + count[p];  // ring step of the last block in this pass
+    // this pass reads gather blocks first[p] .. first[p] + count[p] - 1 = ring steps first[p] + 1 .. + count[p]
+    const int step0 = first[p] + 1;
     int fl = VOMNI_CM_ACC_IN | (p == np - 1 ? (VOMNI_CM_FINAL | flags) : 0);
     if (write_value) {
-      // In-kernel gate on the block's ready word; the pass overlaps the previous pass's last wave
+      // In-kernel gate on the blocks' ready words; the pass overlaps the previous pass's last wave
       // and only its epilogue (the accumulator read-modify-write) waits for that pass.
       fl |= VOMNI_CM_OVERLAP;
     } else {
-      const cudaError_t e = cudaStreamWaitEvent(st, R->ev_block[last_step], 0);
-      if (e != cudaSuccess) {
-        set_last_cuda_error(e);
-        return join_copies(VOMNI_ECUDA);
+      for (int s = step0; s < step0 + count[p]; ++s) {
+        if (const cudaError_t e = cudaStreamWaitEvent(st, R->ev_block[s], 0); e != cudaSuccess) {
+          set_last_cuda_error(e);
+          return join_copies(VOMNI_ECUDA);
+        }
       }
     }
     rc = cm_attend_gated(q, R->gather_k, R->gather_v, b, s_loc, s_kv, first[p] * s_loc, count[p] * s_loc, h, d,
                          q_stride, 0, softmax_scale, R->qn2, R->kmax2, R->acc_o, R->acc_l, fl, out, lse,
-                         write_value ? R->ready + last_step : nullptr, epoch, stream);
+                         write_value ? R->ready + step0 : nullptr, count[p], epoch, stream);
     if (rc) return join_copies(rc);
   }
-  // Join the copy stream: this rank's copies of its peers' send buffers are complete before any later
+  // Join the copy streams: this rank's copies of its peers' send buffers are complete before any later
   // work on the caller stream (the next call's all_reduce included).
   return join_copies(VOMNI_OK);
 }
