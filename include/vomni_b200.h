@@ -285,8 +285,8 @@ VOMNI_API int vomni_ring_check(vomni_ring* ring);
 /* q, k, v: this rank's token-major [b, s_loc, h, d] shard (s_loc <= s_max). out: head-major
  * [b, h, s_loc, d] or d-major with VOMNI_CM_OUT_DMAJOR; lse with VOMNI_CM_LSE.
  * Stream-ordered on `stream`: publishes K/V (on an internal copy stream, overlapping the norms),
- * runs the norms and the key-max all-reduce, pulls the peers' blocks on up to four internal copy
- * streams and runs the attention passes; passes after the first start as programmatic dependents of
+ * runs the norms and the key-max all-reduce, pulls the peers' blocks on an internal copy stream
+ * and runs the attention passes; passes after the first start as programmatic dependents of
  * the previous pass and wait inside the kernel (bounded) for the ready words of all their blocks.
  * Before returning (also on an error) `stream` joins the copy streams. */
 VOMNI_API int vomni_ring_attention(vomni_ring* ring, const void* q, const void* k, const void* v, void* out, float* lse,
