@@ -228,7 +228,7 @@ VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort
     const int valid = p.n_keys - j * kTile;  // keys of this step inside the pass's range
 #pragma unroll
     for (int t = 0; t < kQT; ++t) {
-      if (!mbar_wait(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
+      if (!mbar_wait_spin(&bars[S_FULL + 2 * t], j & 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 7)) { ok = false; break; }
       tc_fence_after();
       if (releaser && t == kQT - 1) release_stage(bars, j);
       const uint32_t col_s = tbase + lane_addr + kColS + t * 128;
@@ -255,7 +255,7 @@ VOMNI_DEV void softmax_role(const Params& p, uint64_t* bars, volatile int* abort
   const bool final_pass = p.flags & VOMNI_CM_FINAL;
 #pragma unroll 1
   for (int t = 0; t < kQT; ++t) {
-    if (!mbar_wait(&bars[O_FULL + t], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) return;
+    if (!mbar_wait_spin(&bars[O_FULL + t], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 9)) return;
     tc_fence_after();
     // A pass launched as a programmatic dependent of the previous pass reads and writes acc / out
     // only from here on, after that pass has completed.
@@ -422,7 +422,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int st = j % kKV;
         const uint32_t ph = (j / kKV) & 1;
         const int k_row = p.k_start + j * kTile;
-        if (j >= kKV && !mbar_wait(&bars[KV_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) break;
+        if (j >= kKV && !mbar_wait_spin(&bars[KV_EMPTY + st], ph ^ 1, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x21)) break;
         if (leader) mbar_expect_tx(&bars[KV_FULL + st], 2 * (kPairKBytes + kPairVBytes));
         tma_load_3d_pair(&tmK, lead_bars + (KV_FULL + st) * 8, sK + st * kPairKBytes, x0, k_row + rank * 64, b);
         tma_load_3d_pair(&tmK, lead_bars + (KV_FULL + st) * 8, sK + st * kPairKBytes + kPairKBytes / 2, x0 + 64,
@@ -442,8 +442,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint64_t k_desc = make_sdesc(smem_u32(sK), 16, 1024, kLayoutSW128);
       const uint64_t v_desc = make_sdesc(smem_u32(sV), kPairVBytes, 1024, kLayoutSW128);
       constexpr uint64_t kTileDesc = kTileBytes >> 4;
-      bool ok = mbar_wait(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x23) &&
-                mbar_wait(&bars[KV_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24);
+      bool ok = mbar_wait_spin(&bars[Q_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x23) &&
+                mbar_wait_spin(&bars[KV_FULL], 0, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < kQT; ++t) {
@@ -463,16 +463,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kQT; ++t) {
           const uint32_t d_o = tbase + kColO + t * 128, d_s = tbase + kColS + t * 128;
           if (kPSets == 2) {
-            if (!mbar_wait(&bars[P_FULL + 2 * t], pphase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
+            if (!mbar_wait_spin(&bars[P_FULL + 2 * t], pphase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
             tc_fence_after();
             issue_pv_pair_chunks<0>(d_o, d_s, vd, acc_first);
           }
-          if (!mbar_wait(&bars[P_FULL + 2 * t + 1], pphase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
+          if (!mbar_wait_spin(&bars[P_FULL + 2 * t + 1], pphase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x25)) { ok = false; break; }
           tc_fence_after();
           if (kPSets == 1) issue_pv_pair_chunks<0>(d_o, d_s, vd, acc_first);
           issue_pv_pair_chunks<1>(d_o, d_s, vd, acc_first);
           if (j < n_tiles) {
-            if (t == 0 && !mbar_wait(&bars[KV_FULL + ks], kv_phase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24)) { ok = false; break; }
+            if (t == 0 && !mbar_wait_spin(&bars[KV_FULL + ks], kv_phase, abort_flag, p.status, VOMNI_DEV_TIMEOUT_BASE + 0x24)) { ok = false; break; }
             tc_fence_after();
             issue_qk_pair(d_s, q_desc + t * kTileDesc, kd);
             tc_commit_pair(&bars[S_FULL + 2 * t]);
